@@ -1,0 +1,390 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the B200 decoder runtime (one JSON line on rank 0).
+
+Workloads (the default is the one its metric is quoted on):
+  cfg2  28-layer Qwen3-0.6B-shaped decoder, FP16 layers + INT8 lm_head,
+        60-token batch prefill of N(0,1) embeddings, then greedy decode at B=1
+        from token 151644.  A step is one decode token.          (default)
+  cfg3  same model quantized W8A16, KV cache pre-filled to --context L.
+  cfg5  batched W4A16 decode of 64 sequences with contexts U[128, 4096],
+        sharded over ranks; a step advances every sequence by one token.
+
+Arms:
+  --impl b200       (default) this runtime.  `value` is device-timed (CUDA
+                    events on the decoder's stream) greedy decode with the token
+                    feedback on the device (matmul_decoder_decode_greedy), inputs
+                    resident in HBM; `e2e` is the same metric through the C API
+                    call a user makes (matmul_decoder_step_token: host->device
+                    parameter block, device->host token id, both inside the
+                    timed region), host-timed.
+  --impl reference  the reference's CPU path (the oracle's scalar C port of
+                    src/cpu_ops.c + the matmul semantics, since the reference
+                    itself needs an ARM NPU) on the host cores with all threads,
+                    rank 0 only.
+
+Multi-GPU (torchrun, one rank per GPU): cfg2/cfg3 run one independent sequence
+per rank (weak scaling, no collective in the data path); cfg5 shards the 64
+sequences over the ranks.  Times are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "rknn-matmul-parallel_b200")
+sys.path.insert(0, os.path.join(PKG, "python"))
+sys.path.insert(0, PKG)
+
+import model_format as mf  # noqa: E402
+
+METRIC = "decode ms/token (B=1) & tok/s (B=64, 1–8 GPU); % of HBM roofline"
+FIRST_TOKEN = 151644
+PREFILL = 60
+
+
+# ─── algorithmic bytes per decode token ───
+
+def layer_weight_bytes(shape: mf.ModelShape, quant: str) -> int:
+    elems = sum(k * n for k, n in shape.proj_shapes().values()) * shape.num_layers
+    n_cols = sum(n for _, n in shape.proj_shapes().values()) * shape.num_layers
+    if quant == "fp16":
+        return elems * 2
+    return (elems if quant == "int8" else elems // 2) + n_cols * 4
+
+
+def token_bytes(shape: mf.ModelShape, quant: str, attended: float) -> float:
+    """Bytes one decode token must move: all layer weights (+scales), the INT8
+    lm_head and its scales, norm weights, the embedding row, the K/V read over
+    `attended` positions and the K/V write of the new position."""
+    H, nl, kvd = shape.hidden_dim, shape.num_layers, shape.num_kv_heads * shape.head_dim
+    lm = shape.vocab_size * H + shape.vocab_size * 4
+    norms = nl * (2 * H + 2 * shape.head_dim) * 4 + H * 4
+    kv = nl * 2 * kvd * 2 * attended + nl * 2 * kvd * 2
+    return layer_weight_bytes(shape, quant) + lm + norms + H * 4 + kv
+
+
+# ─── clocks during the timed region ───
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device: int):
+        self.samples = []
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "20", "-i", str(device)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.p = None
+
+    def _read(self):
+        for line in self.p.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.perf_counter(), parts))
+
+    def stop(self):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        win = [s for t, s in self.samples if t0 - 0.03 <= t <= t1 + 0.03]
+        note = "timed region"
+        if not win:
+            win = [s for _, s in self.samples[-10:]]
+            note = "last samples before the end of the timed region"
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(s[1]) for s in win if num(s[1]) is not None]
+        reasons = set()
+        for s in win:
+            for name, flag in zip(self.NAMES, s[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(win[0][2]),
+                "reasons": sorted(reasons), "samples": len(win), "window": note}
+
+
+# ─── distributed plumbing ───
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, x: float) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_dir(cache: str, quant: str, rank: int, world: int) -> str:
+    shape = mf.ModelShape()
+    d = os.path.join(cache, f"qwen3_0p6b_{quant}")
+    if rank == 0:
+        mf.write_synthetic_model(d, shape, quant=None if quant == "fp16" else quant)
+    barrier(world)
+    return d
+
+
+# ─── CPU baseline (oracle port) ───
+
+def cpu_decode_rate(mdir: str, quant: str, context: int, tokens: int, nthreads: int):
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import ref_decoder as ref
+    dec = ref.RefDecoder(mdir, quant, max_seq_len=context + tokens + 4, nthreads=nthreads)
+    for layer in range(dec.nL):  # seeded context instead of a (slow) CPU prefill
+        k = mf.seeded_kv(mf.kv_seed(layer, 0), context, dec.nkv, dec.hd)
+        v = mf.seeded_kv(mf.kv_seed(layer, 1), context, dec.nkv, dec.hd)
+        dec.set_kv(layer, 0, k, v)
+    dec.seq_len = context
+    tok = FIRST_TOKEN
+    t0 = time.perf_counter()
+    for _ in range(tokens):
+        tok, _ = dec.step(tok)
+    return tokens / (time.perf_counter() - t0)
+
+
+# ─── arms ───
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    import torch  # noqa: F401  (only so the arm's environment matches the b200 arm)
+    nth = os.cpu_count() or 1
+    quant = {"cfg2": "fp16", "cfg3": "int8", "cfg5": "int4"}[args.workload]
+    mdir = model_dir(args.model_cache, quant, 0, 1)
+    context = PREFILL if args.workload == "cfg2" else args.context
+    tokens = args.warmup + args.steps
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import ref_decoder as ref
+    dec = ref.RefDecoder(mdir, quant, max_seq_len=context + tokens + 4, nthreads=nth)
+    for layer in range(dec.nL):
+        dec.set_kv(layer, 0, mf.seeded_kv(mf.kv_seed(layer, 0), context, dec.nkv, dec.hd),
+                   mf.seeded_kv(mf.kv_seed(layer, 1), context, dec.nkv, dec.hd))
+    dec.seq_len = context
+    tok = FIRST_TOKEN
+    for _ in range(args.warmup):
+        tok, _ = dec.step(tok)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok, _ = dec.step(tok)
+    dt = time.perf_counter() - t0
+    rate = args.steps / dt
+    sample = (f"{args.steps} full decode tokens of the 28-layer {quant} model at context {context}"
+              f" (KV seeded), oracle C port, {nth} threads")
+    return {"metric": METRIC, "value": round(rate, 3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights, seeded N(0,1) FP16 KV)", "impl": "reference",
+            "config": {"workload": args.workload, "model": "qwen3-0.6b-shaped", "batch": 1,
+                       "context": context, "quant": quant},
+            "cpu_baseline": {"value": round(rate, 3), "unit": "tok/s", "cores": nth, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(rate, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_single_stream(args, world, rank, local):
+    import b200_decoder as bd
+    quant = "fp16" if args.workload == "cfg2" else "int8"
+    mdir = model_dir(args.model_cache, quant, rank, world)
+    bd.check(bd.capi().b2_set_device(local), "set_device")
+    shape = mf.ModelShape()
+    K, W = args.steps, args.warmup
+    max_seq = PREFILL + max(K, W) + 8 if args.workload == "cfg2" else args.context + max(K, W) + 8
+    dec = bd.Decoder(mdir, quant, max_seq_len=max_seq)
+
+    def reset():
+        bd.capi().matmul_decoder_clear_kv_cache(dec.ctx)
+        if args.workload == "cfg2":
+            dec.prefill_batch(mf.seeded_hidden(820_000, PREFILL, shape.hidden_dim))
+            return PREFILL
+        dec.set_seq_len(args.context)
+        return args.context
+
+    if args.workload == "cfg3":
+        for layer in range(shape.num_layers):
+            dec.set_kv(layer, 0, mf.seeded_kv(mf.kv_seed(layer, 0), args.context, 8, 128),
+                       mf.seeded_kv(mf.kv_seed(layer, 1), args.context, 8, 128))
+    reset()
+    dec.decode_greedy(FIRST_TOKEN, W)  # warm-up: graph capture, clocks, caches
+    ctx0 = reset()
+
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    t0 = time.perf_counter()
+    toks, dev_ms = dec.decode_greedy(FIRST_TOKEN, K)
+    t1 = time.perf_counter()
+    barrier(world)
+    clk = clocks.summary(t0, t1)
+    clocks.stop()
+    ms = max_over_ranks(world, dev_ms)
+
+    # e2e through the C API with host buffers, same context and token count
+    ctx0b = reset()
+    assert ctx0b == ctx0
+    barrier(world)
+    tok = FIRST_TOKEN
+    e0 = time.perf_counter()
+    for _ in range(K):
+        tok = dec.step_token(tok)
+        if tok < 0:
+            raise RuntimeError(f"step_token failed ({tok})")
+    e_s = max_over_ranks(world, time.perf_counter() - e0)
+
+    attended = ctx0 + (K + 1) / 2.0
+    bpt = token_bytes(shape, quant, attended)
+    peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    ms_tok = ms / K
+    achieved = bpt / (ms_tok * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"{args.workload}_bytes_per_token")
+    launches_per_token = 1 + shape.num_layers * 7 + 2 + 1
+    line = {
+        "metric": METRIC, "value": round(world * K / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(ms_tok, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16" if quant == "fp16" else "int8 weights / fp16 act",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) prefill embeddings)",
+        "config": {"workload": args.workload, "model": "qwen3-0.6b-shaped (28 layers, vocab 151936)",
+                   "batch_per_gpu": 1, "context_start": ctx0, "quant": quant, "lm_head": "int8",
+                   "parallelism": f"replicas x{world} (independent sequences)",
+                   "l2": "inputs larger than L2: %.2f GB streamed per token" % (bpt / 1e9)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "whole decode step (CUDA graph)", "bytes_per_token": int(bpt),
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback"},
+        "clocks": clk,
+        "e2e": {"value": round(world * K / e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * (8 + shape.hidden_dim),
+                "d2h_bytes_per_step": 4, "api": "matmul_decoder_step_token (C ABI)"},
+        "gpu_launches": launches_per_token * K,
+        "tokens_check": [int(t) for t in toks[:4]],
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        rate = cpu_decode_rate(mdir, quant, ctx0, args.cpu_tokens, 1)
+        line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+                                "sample": f"{args.cpu_tokens} decode tokens of the same 28-layer model at context "
+                                          f"{ctx0} (KV seeded), oracle scalar C port, 1 thread"}
+    dec.close()
+    return line if rank == 0 else None
+
+
+def run_batched(args, world, rank, local):
+    import b200_decoder as bd
+    mdir = model_dir(args.model_cache, "int4", rank, world)
+    bd.check(bd.capi().b2_set_device(local), "set_device")
+    shape = mf.ModelShape()
+    n_total = args.seqs
+    lens = np.random.default_rng(55).integers(128, 4097, size=n_total)
+    mine = list(range(rank, n_total, world))
+    K, W = args.steps, args.warmup
+    bat = bd.BatchDecoder(mdir, len(mine), "int4", max_seq_len=4096 + K + W + 8)
+
+    def reset():
+        for i, s in enumerate(mine):
+            bat.set_seq_len(i, int(lens[s]))
+    reset()
+    toks = np.full(len(mine), FIRST_TOKEN, np.int32)
+    for _ in range(W):
+        toks = bat.step(toks)
+    reset()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        toks = bat.step(toks)
+    dt = max_over_ranks(world, time.perf_counter() - t0)
+    attended = float(np.mean(lens)) + (K + 1) / 2.0
+    bytes_step = (layer_weight_bytes(shape, "int4") + shape.vocab_size * (shape.hidden_dim + 4)
+                  + n_total * shape.num_layers * 2 * 1024 * 2 * attended / world)
+    line = {"metric": METRIC, "value": round(n_total * K / dt, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(dt * 1e3 / K, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights / fp16 act",
+            "data": "synthetic; KV contents zero (attention cost is value-independent)",
+            "config": {"workload": "cfg5", "sequences": n_total, "per_gpu": len(mine), "context": "U[128,4096]",
+                       "parallelism": f"sequences sharded over {world} GPUs"},
+            "roofline": {"bound": "hbm", "achieved": round(bytes_step / (dt / K) / 1e9, 1), "unit": "GB/s",
+                         "kernel": "batched decode step, host-timed"}}
+    return line if rank == 0 else None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg5"), default="cfg2")
+    ap.add_argument("--context", type=int, default=128, help="cfg3 pre-filled context")
+    ap.add_argument("--seqs", type=int, default=64, help="cfg5 total sequences")
+    ap.add_argument("--model-cache", default=os.environ.get("B2_MODEL_CACHE", "/tmp/b2_bench_models"))
+    ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+        elif args.workload == "cfg5":
+            line = run_batched(args, world, rank, local)
+        else:
+            line = run_single_stream(args, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,236 @@
+/*
+ * b2_kernels.h — thin C-ABI over the sm_100a kernels and the CUDA runtime.
+ *
+ * The host C runtime (libmatmul_decoder.so) reaches the GPU only through these
+ * functions; none of them takes a torch or CUDA C++ type.  Every pointer
+ * documented "device" is device memory of the current CUDA device; "host" is
+ * ordinary or pinned host memory.  Every function returns 0 on success or a
+ * negative MatmulDecoderError (ERR_RKNN = -4 for a CUDA failure,
+ * ERR_INVALID_ARG = -1 for a bad shape); b2_last_error() gives the message.
+ *
+ * Reference interfaces these replace (suharvest/rknn-matmul-parallel):
+ *   b2_gemv            run_persistent_matmul / run_batch_matmul
+ *                      (src/matmul_decoder.c:382-445, :1841-1899) plus the
+ *                      RMSNorm before it and the residual add / SiLU*mul after
+ *                      it (src/cpu_ops.c:18-55, :296-319, :350-359)
+ *   b2_qk_rope_kv      per-head q/k RMSNorm, RoPE, KV store
+ *                      (src/matmul_decoder.c:1495-1516, src/cpu_ops.c:109-155)
+ *   b2_attention       attention_f32 / attention_batch_causal_f32
+ *                      (src/cpu_ops.c:202-264, :459-571)
+ *   b2_lm_head_argmax  final RMSNorm + tiled INT8 lm_head / FP16 / FP32 GEMV
+ *                      + argmax (src/matmul_decoder.c:1563-1633,
+ *                      :1722-1741, src/cpu_ops.c:575-586)
+ *   b2_embed           embedding row copy (src/matmul_decoder.c:1446-1454)
+ *   b2_malloc/...      the NPU buffer pool (rknn_create_mem,
+ *                      src/npu_buffer_pool.c:52-87) becomes a device arena
+ */
+#ifndef B2_KERNELS_H
+#define B2_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b2_stream_s* b2_stream_t;
+typedef struct b2_event_s* b2_event_t;
+typedef struct b2_graph_s* b2_graph_t;
+
+/* Weight encodings in device layout: one row per output column n, K
+ * contiguous.  F16: uint16 [rows][K]; I8: int8 [rows][K]; I4: uint8
+ * [rows][K/2] with element k in byte k/2, low nibble for even k,
+ * two's-complement int4.  I8/I4 rows carry an FP32 scale per row. */
+enum { B2_W_F16 = 0, B2_W_I8 = 1, B2_W_I4 = 2, B2_W_F32 = 3 };
+
+/* GEMV epilogues. */
+enum {
+    B2_EPI_STORE = 0,     /* y[m][n] = acc * s[n]                                   */
+    B2_EPI_ADD = 1,       /* y[m][n] += acc * s[n]   (residual add)                 */
+    B2_EPI_SILU_PAIR = 2, /* rows n and N+n: y[m][n] = silu(g) * u                  */
+};
+
+/* ─── runtime ─── */
+const char* b2_last_error(void);
+int b2_device_count(int* n);
+int b2_set_device(int dev);
+int b2_get_device(int* dev);
+int b2_sm_count(int* n);
+int b2_malloc(void** ptr, size_t bytes);
+int b2_free(void* ptr);
+int b2_host_alloc(void** ptr, size_t bytes);   /* pinned host memory */
+int b2_host_free(void* ptr);
+int b2_mem_get_info(size_t* free_bytes, size_t* total_bytes);
+int b2_memcpy_h2d(void* dst, const void* src, size_t bytes, b2_stream_t s);
+int b2_memcpy_d2h(void* dst, const void* src, size_t bytes, b2_stream_t s);
+int b2_memcpy_d2d(void* dst, const void* src, size_t bytes, b2_stream_t s);
+int b2_memset(void* dst, int value, size_t bytes, b2_stream_t s);
+int b2_stream_create(b2_stream_t* s);
+int b2_stream_destroy(b2_stream_t s);
+int b2_stream_sync(b2_stream_t s);
+int b2_event_create(b2_event_t* e);
+int b2_event_destroy(b2_event_t e);
+int b2_event_record(b2_event_t e, b2_stream_t s);
+int b2_event_elapsed_ms(float* ms, b2_event_t start, b2_event_t stop);
+int b2_graph_begin(b2_stream_t s);
+int b2_graph_end(b2_stream_t s, b2_graph_t* g);
+int b2_graph_launch(b2_graph_t g, b2_stream_t s);
+int b2_graph_destroy(b2_graph_t g);
+
+/* ─── kernels ─── */
+
+/* Weight-only GEMV/skinny GEMM: y[m][n] = epi( s[n] * sum_k f16(xn[m][k]) * W[n][k] )
+ * for m < M, where xn = x, or RMSNorm(x; norm_w, eps) when norm_w != NULL
+ * (computed as (x * rms) * w, rms = 1/sqrtf(mean(x^2) + eps)).  The
+ * activation is rounded to FP16 (round-to-nearest-even) before the multiply
+ * and products accumulate in FP32, like the reference's FP16-input NPU
+ * matmul.  w is the device layout above with N rows (2N for SILU_PAIR, gate
+ * rows first); scales is NULL for F16.  x, y device FP32 with row strides
+ * ldx, ldy (elements). */
+typedef struct {
+    float* y;
+    int ldy;
+    const float* x;
+    int ldx;
+    int M, K, N;
+    const void* w;
+    const float* scales;
+    int wtype;
+    const float* norm_w;
+    float eps;
+    int epilogue;
+} B2GemvArgs;
+int b2_gemv(const B2GemvArgs* a, b2_stream_t s);
+
+/* Embedding: for row m, hidden[m] = use_staged && *use_staged ? staged[m]
+ * : table[tokens[m]].  tokens, use_staged, staged are device pointers
+ * (use_staged/staged may be NULL). */
+int b2_embed(float* hidden, const float* table, const int* tokens, const int* use_staged,
+             const float* staged, int M, int dim, b2_stream_t s);
+
+/* KV cache addressing: the cache of (sequence q, layer l) starts at
+ * base + q * seq_stride + l * layer_stride elements and is laid out
+ * [num_kv_heads][max_seq][head_dim] FP16.  rows[m] gives the sequence of
+ * row m (NULL = sequence 0) and pos[m] its position.  A row whose position is
+ * outside [0, max_seq) or whose sequence is outside [0, n_seqs) is skipped by
+ * the kernels (no cache access; its attention output is NaN). */
+typedef struct {
+    uint16_t* k_base;
+    uint16_t* v_base;
+    long long seq_stride;
+    long long layer_stride;
+    int layer;
+    int max_seq;
+    const int* rows_seq;
+    const int* pos;
+    int n_seqs;
+} B2KVRef;
+
+/* Per-head q/k RMSNorm (q_norm_w/k_norm_w may be NULL), RoPE from tables
+ * cos/sin [max_seq][hd/2] at pos[m] (style 0 interleaved, 1 split-half),
+ * then K and V of row m stored as FP16 at pos[m].  qkv: device FP32
+ * [M][ldqkv] = [q (nq*hd) | k (nkv*hd) | v (nkv*hd)]; q is updated in place. */
+int b2_qk_rope_kv(float* qkv, int ldqkv, int M, int nq, int nkv, int hd,
+                  const float* q_norm_w, const float* k_norm_w, float eps,
+                  const float* cos_tab, const float* sin_tab, int rope_style,
+                  const B2KVRef* kv, b2_stream_t s);
+
+/* GQA attention of row m over cache positions [0, pos[m]] (inclusive).
+ * q device FP32 [M][ldq] (first nq*hd), out device FP32 [M][nq*hd].
+ * work: device scratch of at least b2_attention_workspace(M, nq, hd, nsplit)
+ * bytes; nsplit <= 0 picks a split count. */
+size_t b2_attention_workspace(int M, int nq, int hd, int nsplit);
+int b2_attention(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                 const B2KVRef* kv, void* work, int nsplit, b2_stream_t s);
+
+/* lm_head + argmax over V rows of `table` (int8 [V][K] with FP32 scales,
+ * F16 [V][K], or F32 [V][K]).  Input row m is RMSNorm(x[m]; norm_w, eps)
+ * (norm_w may be NULL), rounded to FP16 for the int8 table (the reference's
+ * NPU path) and kept FP32 for the F16/F32 tables (its CPU GEMV path).
+ * logits (device, may be NULL) get [M][ldl]; tokens (device int32 [M]) get
+ * the first index of the maximum.  work: b2_lm_head_workspace(M, V) bytes. */
+size_t b2_lm_head_workspace(int M, int V);
+int b2_lm_head_argmax(const float* x, int ldx, int M, int K, int V, const void* table,
+                      const float* scales, int wtype, const float* norm_w, float eps,
+                      float* logits, int ldl, int* tokens, void* work, b2_stream_t s);
+
+/* Device-side greedy loop bookkeeping, run once per step after the argmax:
+ * hist[loop[2]] = loop[0] (the token just produced, which is also the next
+ * step's input), then loop[1] (position) and loop[2] (step counter) advance.
+ * loop and hist are device int32. */
+int b2_loop_advance(int* loop, int* hist, int hist_len, b2_stream_t s);
+
+/* ─── persistent single-token decode (one launch = one token) ───
+ * The whole decode step — embedding, every layer, and optionally final norm +
+ * INT8 lm_head + argmax — as one cooperative kernel with one CTA per SM.  A
+ * producer warp per CTA streams that CTA's weight rows (and K/V positions
+ * written by earlier steps) through a shared-memory ring with bulk copies;
+ * the other warps compute and order the dependent phases with device-scope
+ * acquire/release counters.  Every wait is bounded: on timeout the kernel
+ * sets state[B2_MK_ERR], drains its copies and returns.
+ *
+ * Device state block (int32): */
+enum {
+    B2_MK_TOKEN = 0,     /* in: token id of this step (ignored when USE_EMB) */
+    B2_MK_POS = 1,       /* in/out: position; +1 per completed step          */
+    B2_MK_STEP = 2,      /* in/out: step counter (index into hist)           */
+    B2_MK_USE_EMB = 3,   /* in: 1 = take the input row from staged_emb       */
+    B2_MK_ERR = 4,       /* out: nonzero after a timed-out wait              */
+    B2_MK_TOKEN_OUT = 5, /* out: argmax of this step (also written to TOKEN) */
+    B2_MK_GEN = 6,       /* device-owned generation count; host leaves it    */
+    B2_MK_STATE_INTS = 16
+};
+#define B2_MK_MAX_LAYERS 48
+
+typedef struct {
+    const void* qkv;       /* [nq*hd + 2*nkv*hd][hidden] rows               */
+    const float* qkv_s;
+    const void* o;         /* [hidden][nq*hd]                               */
+    const float* o_s;
+    const void* gu;        /* [2*ffn][hidden]: gate rows then up rows       */
+    const float* gu_s;
+    const void* dn;        /* [hidden][ffn]                                 */
+    const float* dn_s;
+    const float* in_norm;
+    const float* post_norm;
+    const float* q_norm;   /* NULL when the model has no q/k norm           */
+    const float* k_norm;
+} B2MkLayer;
+
+typedef struct {
+    int n_layers, hidden, nq, nkv, hd, ffn, vocab, max_seq, rope_style, wtype;
+    float eps;
+    const float* emb;          /* [vocab][hidden] FP32                        */
+    const void* lm;            /* [vocab][hidden] int8                        */
+    const float* lm_s;
+    const float* final_norm;
+    const float* cos_tab;      /* [max_seq][hd/2]                             */
+    const float* sin_tab;
+    uint16_t* k_cache;         /* [layer][nkv][max_seq][hd] FP16              */
+    uint16_t* v_cache;
+    long long layer_stride;    /* elements per layer of k_cache / v_cache     */
+    int* state;                /* B2_MK_STATE_INTS ints                       */
+    const float* staged_emb;   /* [hidden] input row when USE_EMB             */
+    float* logits;             /* [vocab] or NULL                             */
+    int* hist;                 /* tokens by step (device loop), or NULL       */
+    int hist_len;
+    int do_lm;                 /* 0 = prefill-mode step (no final norm/lm_head) */
+    void* scratch;             /* b2_mk_scratch_bytes() bytes, zeroed once    */
+    B2MkLayer layer[B2_MK_MAX_LAYERS];
+} B2MkPlan;
+
+/* 0 when the plan's shapes are supported by the persistent kernel. */
+int b2_mk_check(const B2MkPlan* plan);
+size_t b2_mk_scratch_bytes(int n_layers, int hidden, int ffn, int nq, int nkv, int hd);
+int b2_mk_decode(const B2MkPlan* plan, b2_stream_t s);
+/* Device address of the residual stream after the last layer of the most
+ * recent step (inside plan->scratch). */
+float* b2_mk_final_hidden(const B2MkPlan* plan);
+/* Dynamic shared memory of one CTA of the persistent kernel. */
+size_t b2_mk_smem_bytes(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -299,6 +299,15 @@ int matmul_decoder_export_hf_model(const char* hf_model_path,
 int matmul_decoder_step_token(MatmulDecoderContext* ctx, int token_id,
                               const float* embedding);
 
+/* ADDITIVE.  Greedy decode of n_tokens tokens with the token feedback kept on
+ * the device: step i consumes the token produced by step i-1 (step 0 consumes
+ * first_token), so the host neither copies a token nor synchronizes between
+ * steps.  tokens_out (host, n_tokens) gets the produced tokens; device_ms
+ * (optional) gets the GPU time of the n_tokens steps measured with CUDA
+ * events on the decoder's stream.  Returns n_tokens or a negative error. */
+int matmul_decoder_decode_greedy(MatmulDecoderContext* ctx, int first_token, int n_tokens,
+                                 int* tokens_out, float* device_ms);
+
 /* ADDITIVE.  Write positions [start, start+len) of one layer's KV cache from
  * host FP16 bits laid out [len][num_kv_heads][head_dim] (the reference cache's
  * position-major order).  Does not change seq_len. */
@@ -314,7 +323,8 @@ int matmul_decoder_get_kv(MatmulDecoderContext* ctx, int layer, int start, int l
 int matmul_decoder_set_seq_len(MatmulDecoderContext* ctx, int n);
 
 /* ADDITIVE.  Copy the residual-stream hidden state after the last layer of
- * the most recent step (before the final norm) to host FP32 [hidden_dim]. */
+ * the most recent token (the step's token, or the last row of the last
+ * prefill_batch), before the final norm, to host FP32 [hidden_dim]. */
 int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out);
 
 /* ADDITIVE.  Quantize one FP16 [K][N] weight on the host into the on-disk
@@ -323,6 +333,13 @@ int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out);
  * reference's per-column rule (max|col| / qmax, roundf, clamp). */
 int matmul_decoder_quantize_weight(const uint16_t* w_fp16, int K, int N, int bits,
                                    uint8_t* q_out, float* scales_out);
+
+/* ADDITIVE.  The INT8 lm_head the decoder builds at create time, computed on
+ * the host: the FP32 [V][K] table is rounded to FP16, then each vocab row is
+ * quantized with the reference rule (max|row| / 127, roundf, clamp to
+ * [-128, 127]).  q_out gets int8 [V][K]; scales_out gets FP32 [V]. */
+int matmul_decoder_quantize_lm_head(const float* table, int V, int K, int8_t* q_out,
+                                    float* scales_out);
 
 /* ─── ADDITIVE: batched multi-sequence decode ───
  * n_seqs independent sequences share one copy of the weights; each has its own

@@ -1,0 +1,264 @@
+/*
+ * Batched multi-sequence decode (ADDITIVE entry points of matmul_decoder.h).
+ *
+ * The reference decodes one sequence per context (matmul_decoder_step,
+ * src/matmul_decoder.c:1430-1634).  Here n_seqs independent sequences share
+ * one device copy of the weights; each has its own FP16 KV cache
+ * [layer][kv_head][pos][hd] and position.  One step is one CUDA graph replay
+ * over all sequences as the rows of a skinny GEMM: the weights stream once
+ * per step for every sequence, attention reads each row's own cache up to its
+ * own position, and the lm_head + argmax produce one token per sequence.
+ * Token ids and positions travel in a small pinned block per step.
+ */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "md_internal.h"
+
+struct MatmulDecoderBatch {
+    DevModel model;
+    int device, n, max_seq, split;
+    b2_stream_t stream;
+    uint16_t *k_cache, *v_cache;
+    long long seq_stride, layer_stride;
+    float *hidden, *qkv, *attn, *act, *logits;
+    int *d_blk;   /* [0,n) tokens, [n,2n) positions, [2n,3n) row->sequence */
+    int *d_tok;
+    void *attn_work, *lm_work;
+    int *h_blk, *h_tok;
+    int* seq_len;
+    b2_graph_t graph;
+    b2_event_t ev[3];
+    MatmulDecoderStats stats;
+};
+
+static double now_ms(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec / 1e6;
+}
+
+static size_t batch_bytes(const MatmulDecoderConfig* c, int n, int max_seq, int split) {
+    const size_t H = c->hidden_dim, hd = c->head_dim, qd = (size_t)c->num_q_heads * hd;
+    const size_t kvd = (size_t)c->num_kv_heads * hd, F = c->ffn_dim;
+    size_t t = 2 * (size_t)n * c->num_layers * kvd * (size_t)max_seq * 2;
+    t += (size_t)n * (H + qd + 2 * kvd + qd + F) * 4 + (size_t)n * c->vocab_size * 4 + 16 * 256;
+    t += (size_t)n * 3 * 4 + 1024;
+    t += b2_attention_workspace(n, c->num_q_heads, (int)hd, split) + b2_lm_head_workspace(n, c->vocab_size);
+    return t + 4096;
+}
+
+void matmul_decoder_batch_destroy(MatmulDecoderBatch* b) {
+    if (!b) return;
+    b2_set_device(b->device);
+    if (b->stream) b2_stream_sync(b->stream);
+    b2_graph_destroy(b->graph);
+    for (int i = 0; i < 3; i++) b2_event_destroy(b->ev[i]);
+    b2_stream_destroy(b->stream);
+    b2_host_free(b->h_blk);
+    b2_host_free(b->h_tok);
+    free(b->seq_len);
+    md_model_free(&b->model);
+    free(b);
+}
+
+MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const MatmulDecoderConfig* config,
+                                                QuantizationType quant_type, int max_seq_len, int n_seqs) {
+    if (!model_dir || n_seqs <= 0 || n_seqs > 4096) return NULL;
+    MatmulDecoderConfig cfg;
+    if (config) {
+        cfg = *config;
+    } else {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/config.json", model_dir);
+        if (matmul_decoder_load_config(path, &cfg) != 0) return NULL;
+    }
+    if (cfg.num_lm_heads > 1) {
+        MD_LOG("batched decode supports single-head models\n");
+        return NULL;
+    }
+    if (max_seq_len <= 0) max_seq_len = cfg.max_seq_len > 0 ? cfg.max_seq_len : 4096;
+    MatmulDecoderBatch* b = (MatmulDecoderBatch*)calloc(1, sizeof(*b));
+    if (!b) return NULL;
+    b->n = n_seqs;
+    b->max_seq = max_seq_len;
+    int sm = 148;
+    b2_sm_count(&sm);
+    b->split = (2 * sm + n_seqs * cfg.num_kv_heads - 1) / (n_seqs * cfg.num_kv_heads);
+    if (b->split < 1) b->split = 1;
+    if (b->split > 64) b->split = 64;
+    b2_get_device(&b->device);
+    b->seq_len = (int*)calloc((size_t)n_seqs, sizeof(int));
+    int rc = b->seq_len ? 0 : MATMUL_DECODER_ERR_MEMORY;
+    if (!rc)
+        rc = md_model_load_dir(&b->model, model_dir, &cfg, quant_type, max_seq_len,
+                               batch_bytes(&cfg, n_seqs, max_seq_len, b->split));
+    if (rc) {
+        MD_LOG("batch_create failed (%d)\n", rc);
+        matmul_decoder_batch_destroy(b);
+        return NULL;
+    }
+    DevModel* m = &b->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    const size_t H = c->hidden_dim, hd = c->head_dim, qd = (size_t)c->num_q_heads * hd;
+    const size_t kvd = (size_t)c->num_kv_heads * hd, F = c->ffn_dim, n = (size_t)n_seqs;
+    b->layer_stride = (long long)kvd * max_seq_len;
+    b->seq_stride = b->layer_stride * c->num_layers;
+    const size_t kv_bytes = n * c->num_layers * kvd * (size_t)max_seq_len * 2;
+    b->k_cache = (uint16_t*)md_arena_alloc(&m->arena, kv_bytes);
+    b->v_cache = (uint16_t*)md_arena_alloc(&m->arena, kv_bytes);
+    b->hidden = (float*)md_arena_alloc(&m->arena, n * H * 4);
+    b->qkv = (float*)md_arena_alloc(&m->arena, n * (qd + 2 * kvd) * 4);
+    b->attn = (float*)md_arena_alloc(&m->arena, n * qd * 4);
+    b->act = (float*)md_arena_alloc(&m->arena, n * F * 4);
+    b->logits = (float*)md_arena_alloc(&m->arena, n * c->vocab_size * 4);
+    b->d_blk = (int*)md_arena_alloc(&m->arena, n * 3 * 4);
+    b->d_tok = (int*)md_arena_alloc(&m->arena, n * 4);
+    b->attn_work = md_arena_alloc(&m->arena, b2_attention_workspace(n_seqs, c->num_q_heads, (int)hd, b->split));
+    b->lm_work = md_arena_alloc(&m->arena, b2_lm_head_workspace(n_seqs, c->vocab_size));
+    if (!b->k_cache || !b->v_cache || !b->hidden || !b->qkv || !b->attn || !b->act || !b->logits || !b->d_blk ||
+        !b->d_tok || !b->attn_work || !b->lm_work)
+        rc = MATMUL_DECODER_ERR_MEMORY;
+    if (!rc) rc = b2_memset(b->k_cache, 0, kv_bytes, NULL);
+    if (!rc) rc = b2_memset(b->v_cache, 0, kv_bytes, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    if (!rc) rc = b2_stream_create(&b->stream);
+    for (int i = 0; i < 3 && !rc; i++) rc = b2_event_create(&b->ev[i]);
+    if (!rc) rc = b2_host_alloc((void**)&b->h_blk, n * 3 * 4);
+    if (!rc) rc = b2_host_alloc((void**)&b->h_tok, n * 4);
+    if (rc) {
+        MD_LOG("batch_create allocation failed (%d): %s\n", rc, b2_last_error());
+        matmul_decoder_batch_destroy(b);
+        return NULL;
+    }
+    for (int i = 0; i < n_seqs; i++) b->h_blk[2 * n_seqs + i] = i;
+    printf("[MatmulDecoder] Batch ready: %d sequences, max_seq=%d, arena %.1f GB\n", n_seqs, max_seq_len,
+           m->arena.size / 1e9);
+    return b;
+}
+
+int matmul_decoder_batch_set_kv(MatmulDecoderBatch* b, int seq, int layer, int start, int len,
+                                const uint16_t* k_fp16, const uint16_t* v_fp16) {
+    if (!b || seq < 0 || seq >= b->n) return MATMUL_DECODER_ERR_INVALID_ARG;
+    const MatmulDecoderConfig* c = &b->model.cfg;
+    if (layer < 0 || layer >= c->num_layers || start < 0 || len <= 0 || start + len > b->max_seq || !k_fp16 ||
+        !v_fp16)
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    b2_set_device(b->device);
+    const int nkv = c->num_kv_heads, hd = c->head_dim;
+    uint16_t* tmp = (uint16_t*)malloc((size_t)len * nkv * hd * 2);
+    if (!tmp) return MATMUL_DECODER_ERR_MEMORY;
+    int rc = 0;
+    for (int which = 0; which < 2 && !rc; which++) {
+        const uint16_t* host = which ? v_fp16 : k_fp16;
+        uint16_t* dev = (which ? b->v_cache : b->k_cache) + seq * b->seq_stride + layer * b->layer_stride;
+        for (int g = 0; g < nkv; g++)
+            for (int p = 0; p < len; p++)
+                memcpy(tmp + ((size_t)g * len + p) * hd, host + ((size_t)p * nkv + g) * hd, (size_t)hd * 2);
+        for (int g = 0; g < nkv && !rc; g++)
+            rc = b2_memcpy_h2d(dev + ((size_t)g * b->max_seq + start) * hd, tmp + (size_t)g * len * hd,
+                               (size_t)len * hd * 2, b->stream);
+        if (!rc) rc = b2_stream_sync(b->stream);
+    }
+    free(tmp);
+    return rc;
+}
+
+int matmul_decoder_batch_set_seq_len(MatmulDecoderBatch* b, int seq, int n) {
+    if (!b || seq < 0 || seq >= b->n || n < 0 || n > b->max_seq) return MATMUL_DECODER_ERR_INVALID_ARG;
+    b->seq_len[seq] = n;
+    return MATMUL_DECODER_OK;
+}
+
+int matmul_decoder_batch_get_seq_len(const MatmulDecoderBatch* b, int seq) {
+    if (!b || seq < 0 || seq >= b->n) return MATMUL_DECODER_ERR_INVALID_ARG;
+    return b->seq_len[seq];
+}
+
+static int batch_enqueue(MatmulDecoderBatch* b) {
+    DevModel* m = &b->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    const int H = c->hidden_dim, n = b->n;
+    b2_stream_t s = b->stream;
+    int rc = b2_memcpy_h2d(b->d_blk, b->h_blk, (size_t)n * 3 * 4, s);
+    if (!rc) rc = b2_event_record(b->ev[0], s);
+    if (!rc) rc = b2_embed(b->hidden, m->emb, b->d_blk, NULL, NULL, n, H, s);
+    B2KVRef kv = {b->k_cache, b->v_cache, b->seq_stride, b->layer_stride, 0, b->max_seq, b->d_blk + 2 * n,
+                  b->d_blk + n, n};
+    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split};
+    if (!rc) rc = md_enqueue_layers(m, &lb, n, &kv, s);
+    if (!rc) rc = b2_event_record(b->ev[1], s);
+    if (!rc)
+        rc = b2_lm_head_argmax(b->hidden, H, n, H, c->vocab_size, m->lm, m->lm_scales, m->lm_wtype, m->final_norm,
+                               c->rms_eps, b->logits, c->vocab_size, b->d_tok, b->lm_work, s);
+    if (!rc) rc = b2_memcpy_d2h(b->h_tok, b->d_tok, (size_t)n * 4, s);
+    if (!rc) rc = b2_event_record(b->ev[2], s);
+    return rc;
+}
+
+int matmul_decoder_batch_step(MatmulDecoderBatch* b, const int* tokens_in, int* tokens_out, float* logits_out) {
+    if (!b || !tokens_in || !tokens_out) return MATMUL_DECODER_ERR_INVALID_ARG;
+    const MatmulDecoderConfig* c = &b->model.cfg;
+    for (int i = 0; i < b->n; i++) {
+        if (tokens_in[i] < 0 || tokens_in[i] >= c->vocab_size) return MATMUL_DECODER_ERR_INVALID_ARG;
+        if (b->seq_len[i] >= b->max_seq) {
+            MD_LOG("KV cache full for sequence %d\n", i);
+            return MATMUL_DECODER_ERR_INVALID_ARG;
+        }
+    }
+    const double t0 = now_ms();
+    b2_set_device(b->device);
+    int rc = 0;
+    if (!b->graph) {
+        rc = b2_graph_begin(b->stream);
+        if (rc) return rc;
+        int rc2 = batch_enqueue(b);
+        b2_graph_t g = NULL;
+        rc = b2_graph_end(b->stream, &g);
+        if (rc2 || rc) {
+            b2_graph_destroy(g);
+            MD_LOG("batch graph capture failed: %s\n", b2_last_error());
+            return rc2 ? rc2 : rc;
+        }
+        b->graph = g;
+    }
+    for (int i = 0; i < b->n; i++) {
+        b->h_blk[i] = tokens_in[i];
+        b->h_blk[b->n + i] = b->seq_len[i];
+    }
+    rc = b2_graph_launch(b->graph, b->stream);
+    if (!rc) rc = b2_stream_sync(b->stream);
+    if (rc) {
+        MD_LOG("batch step failed: %s\n", b2_last_error());
+        return rc;
+    }
+    double t_copy = 0;
+    if (logits_out) {
+        const double tc = now_ms();
+        rc = b2_memcpy_d2h(logits_out, b->logits, (size_t)b->n * c->vocab_size * 4, b->stream);
+        if (!rc) rc = b2_stream_sync(b->stream);
+        if (rc) return rc;
+        t_copy = now_ms() - tc;
+    }
+    for (int i = 0; i < b->n; i++) {
+        tokens_out[i] = b->h_tok[i];
+        b->seq_len[i]++;
+    }
+    float lay = 0, head = 0;
+    b2_event_elapsed_ms(&lay, b->ev[0], b->ev[1]);
+    b2_event_elapsed_ms(&head, b->ev[1], b->ev[2]);
+    b->stats.total_ms = (float)(now_ms() - t0);
+    b->stats.matmul_ms = lay;
+    b->stats.lm_head_ms = head;
+    b->stats.convert_ms = (float)t_copy;
+    b->stats.rebind_ms = 0;
+    b->stats.cpu_ops_ms = 0;
+    b->stats.n_steps++;
+    return MATMUL_DECODER_OK;
+}
+
+void matmul_decoder_batch_get_stats(const MatmulDecoderBatch* b, MatmulDecoderStats* stats) {
+    if (b && stats) *stats = b->stats;
+}

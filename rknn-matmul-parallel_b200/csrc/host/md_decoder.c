@@ -1,0 +1,736 @@
+/*
+ * Decoder context: create / step / prefill / KV / stats (the reference C API,
+ * src/matmul_decoder.c:830-2180 of suharvest/rknn-matmul-parallel).
+ *
+ * Device residency: weights, the FP16 KV cache [layer][kv_head][pos][hd],
+ * RoPE tables and every activation live in one device arena.  A decode step
+ * is one CUDA graph replay: a host->device copy of a small pinned parameter
+ * block (token id, "use embedding" flag, position, optional embedding), the
+ * embedding gather, all layers, then (unless in prefill mode) the final norm,
+ * the lm_head and the on-device argmax, and a 4-byte device->host copy of the
+ * token.  The graph reads the position from device memory, so one graph
+ * serves every position.  Logits cross to the host only when the caller
+ * passes a logits buffer.
+ *
+ * When the shapes allow it (INT8 lm_head, GQA group <= 2, head_dim 128), a
+ * single-token step runs instead as ONE launch of the persistent decode
+ * kernel (b2_mk_decode), which streams the whole token's weights from one
+ * CTA per SM.  B2_DECODE_KERNEL=graph in the environment at create time
+ * selects the multi-kernel graph instead.  Batch prefill always uses the
+ * multi-kernel pass.
+ */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "md_internal.h"
+
+#define PARAMS_INTS 8 /* [0] token, [1] use_embedding, [4] position */
+
+struct MatmulDecoderContext {
+    DevModel model;
+    MatmulDecoderConfig config;
+    int device, max_seq, seq_len, rows_cap, split_decode;
+    int hidden_row; /* row of `hidden` holding the most recent token */
+    b2_stream_t stream;
+    uint16_t *k_cache, *v_cache;
+    long long layer_stride;
+    float *hidden, *qkv, *attn, *act, *logits;
+    int* d_blk;    /* PARAMS_INTS ints then hidden_dim floats */
+    int* d_pos;    /* [rows_cap] prefill positions */
+    int* d_tok;
+    int* d_loop;   /* device greedy loop: [0] token, [1] position, [2] step */
+    int* d_hist;   /* [max_seq] tokens produced by the device loop */
+    void *attn_work, *lm_work;
+    int* h_blk;    /* pinned mirror of d_blk */
+    int* h_tok;    /* pinned */
+    int* h_pos;    /* pinned [rows_cap] */
+    int* h_loop;   /* pinned [4] */
+    b2_graph_t g_head, g_nohead, g_loop;
+    int use_mk;       /* persistent decode kernel selected */
+    int hidden_mk;    /* last token's hidden lives in the persistent kernel's scratch */
+    B2MkPlan mk;
+    int* d_mk_state;  /* B2_MK_STATE_INTS */
+    int* h_mk_state;  /* pinned mirror */
+    void* mk_scratch;
+    b2_event_t ev[3];
+    MatmulDecoderStats stats;
+};
+
+static double now_ms(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec / 1e6;
+}
+
+static int fail(const char* what, int rc) {
+    MD_LOG("%s failed (%d): %s\n", what, rc, b2_last_error());
+    return rc;
+}
+
+/* ─── creation ─── */
+
+static size_t ctx_bytes(const MatmulDecoderConfig* c, int max_seq, int rows_cap, int split_decode) {
+    const size_t H = c->hidden_dim, hd = c->head_dim, qd = (size_t)c->num_q_heads * hd;
+    const size_t kvd = (size_t)c->num_kv_heads * hd, F = c->ffn_dim;
+    size_t vmax = c->vocab_size;
+    if (c->num_lm_heads > 1 && (size_t)c->lm_head_vocab_size > vmax) vmax = c->lm_head_vocab_size;
+    size_t t = 2 * (size_t)c->num_layers * kvd * (size_t)max_seq * 2;   /* KV cache */
+    t += (size_t)rows_cap * (H + qd + 2 * kvd + qd + F) * 4 + 8 * 256;   /* activations */
+    t += vmax * 4 + (PARAMS_INTS + H) * 4 + (size_t)rows_cap * 4 + 1024;
+    size_t aw1 = b2_attention_workspace(1, c->num_q_heads, (int)hd, split_decode);
+    size_t aw2 = b2_attention_workspace(rows_cap, c->num_q_heads, (int)hd, 1);
+    t += (aw1 > aw2 ? aw1 : aw2) + b2_lm_head_workspace(1, (int)vmax) + 1024;
+    t += 256 + (size_t)max_seq * 4 + 256;
+    t += 256 + b2_mk_scratch_bytes(c->num_layers, (int)H, (int)F, c->num_q_heads, c->num_kv_heads, (int)hd) + 256;
+    return t;
+}
+
+static int ctx_alloc(MatmulDecoderContext* ctx) {
+    DevModel* m = &ctx->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    const size_t H = c->hidden_dim, hd = c->head_dim, qd = (size_t)c->num_q_heads * hd;
+    const size_t kvd = (size_t)c->num_kv_heads * hd, F = c->ffn_dim;
+    size_t vmax = c->vocab_size;
+    if (c->num_lm_heads > 1 && (size_t)c->lm_head_vocab_size > vmax) vmax = c->lm_head_vocab_size;
+    ctx->layer_stride = (long long)kvd * ctx->max_seq;
+    const size_t kv_bytes = (size_t)c->num_layers * kvd * ctx->max_seq * 2;
+    ctx->k_cache = (uint16_t*)md_arena_alloc(&m->arena, kv_bytes);
+    ctx->v_cache = (uint16_t*)md_arena_alloc(&m->arena, kv_bytes);
+    ctx->hidden = (float*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * H * 4);
+    ctx->qkv = (float*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * (qd + 2 * kvd) * 4);
+    ctx->attn = (float*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * qd * 4);
+    ctx->act = (float*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * F * 4);
+    ctx->logits = (float*)md_arena_alloc(&m->arena, vmax * 4);
+    ctx->d_blk = (int*)md_arena_alloc(&m->arena, (PARAMS_INTS + H) * 4);
+    ctx->d_pos = (int*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * 4);
+    ctx->d_tok = (int*)md_arena_alloc(&m->arena, 64);
+    size_t aw1 = b2_attention_workspace(1, c->num_q_heads, (int)hd, ctx->split_decode);
+    size_t aw2 = b2_attention_workspace(ctx->rows_cap, c->num_q_heads, (int)hd, 1);
+    ctx->attn_work = md_arena_alloc(&m->arena, aw1 > aw2 ? aw1 : aw2);
+    ctx->lm_work = md_arena_alloc(&m->arena, b2_lm_head_workspace(1, (int)vmax));
+    ctx->d_loop = (int*)md_arena_alloc(&m->arena, 64);
+    ctx->d_hist = (int*)md_arena_alloc(&m->arena, (size_t)ctx->max_seq * 4);
+    if (!ctx->d_loop || !ctx->d_hist) return MATMUL_DECODER_ERR_MEMORY;
+    const size_t mk_bytes =
+        b2_mk_scratch_bytes(c->num_layers, (int)H, (int)F, c->num_q_heads, c->num_kv_heads, (int)hd);
+    ctx->d_mk_state = (int*)md_arena_alloc(&m->arena, B2_MK_STATE_INTS * 4);
+    ctx->mk_scratch = md_arena_alloc(&m->arena, mk_bytes);
+    if (!ctx->d_mk_state || !ctx->mk_scratch) return MATMUL_DECODER_ERR_MEMORY;
+    if (b2_memset(ctx->d_mk_state, 0, B2_MK_STATE_INTS * 4, NULL) || b2_memset(ctx->mk_scratch, 0, mk_bytes, NULL))
+        return MATMUL_DECODER_ERR_RKNN;
+    if (!ctx->k_cache || !ctx->v_cache || !ctx->hidden || !ctx->qkv || !ctx->attn || !ctx->act ||
+        !ctx->logits || !ctx->d_blk || !ctx->d_pos || !ctx->d_tok || !ctx->attn_work || !ctx->lm_work)
+        return MATMUL_DECODER_ERR_MEMORY;
+    int rc = b2_memset(ctx->k_cache, 0, kv_bytes, NULL);
+    if (!rc) rc = b2_memset(ctx->v_cache, 0, kv_bytes, NULL);
+    if (!rc) rc = b2_memset(ctx->d_blk, 0, (PARAMS_INTS + H) * 4, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    if (!rc) rc = b2_stream_create(&ctx->stream);
+    for (int i = 0; i < 3 && !rc; i++) rc = b2_event_create(&ctx->ev[i]);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_blk, (PARAMS_INTS + H) * 4);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_tok, 64);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_pos, (size_t)ctx->rows_cap * 4);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_loop, 64);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_mk_state, B2_MK_STATE_INTS * 4);
+    if (!rc) memset(ctx->h_blk, 0, (PARAMS_INTS + H) * 4);
+    return rc;
+}
+
+static MatmulDecoderContext* ctx_new(const MatmulDecoderConfig* cfg, int max_seq) {
+    MatmulDecoderContext* ctx = (MatmulDecoderContext*)calloc(1, sizeof(*ctx));
+    if (!ctx) return NULL;
+    ctx->max_seq = max_seq;
+    ctx->rows_cap = 512;
+    int sm = 148;
+    b2_sm_count(&sm);
+    ctx->split_decode = (2 * sm + cfg->num_kv_heads - 1) / cfg->num_kv_heads;
+    if (ctx->split_decode > 64) ctx->split_decode = 64;
+    b2_get_device(&ctx->device);
+    return ctx;
+}
+
+/* Fill the persistent-kernel plan; selects it when the shapes are supported. */
+static void mk_setup(MatmulDecoderContext* ctx) {
+    const char* env = getenv("B2_DECODE_KERNEL");
+    DevModel* m = &ctx->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    if ((env && strcmp(env, "graph") == 0) || m->n_lm_heads > 1 || m->lm_wtype != B2_W_I8 ||
+        c->num_layers > B2_MK_MAX_LAYERS)
+        return;
+    B2MkPlan* p = &ctx->mk;
+    memset(p, 0, sizeof(*p));
+    p->n_layers = c->num_layers;
+    p->hidden = c->hidden_dim;
+    p->nq = c->num_q_heads;
+    p->nkv = c->num_kv_heads;
+    p->hd = c->head_dim;
+    p->ffn = c->ffn_dim;
+    p->vocab = c->vocab_size;
+    p->max_seq = ctx->max_seq;
+    p->rope_style = c->rope_style;
+    p->wtype = m->wtype;
+    p->eps = c->rms_eps;
+    p->emb = m->emb;
+    p->lm = m->lm;
+    p->lm_s = m->lm_scales;
+    p->final_norm = m->final_norm;
+    p->cos_tab = m->cos_tab;
+    p->sin_tab = m->sin_tab;
+    p->k_cache = ctx->k_cache;
+    p->v_cache = ctx->v_cache;
+    p->layer_stride = ctx->layer_stride;
+    p->state = ctx->d_mk_state;
+    p->staged_emb = (const float*)(ctx->d_blk + PARAMS_INTS);
+    p->logits = ctx->logits;
+    p->hist = ctx->d_hist;
+    p->hist_len = ctx->max_seq;
+    p->do_lm = 1;
+    p->scratch = ctx->mk_scratch;
+    for (int l = 0; l < c->num_layers; l++) {
+        const DevLayer* L = &m->layers[l];
+        B2MkLayer* d = &p->layer[l];
+        d->qkv = L->qkv.w;
+        d->qkv_s = L->qkv.s;
+        d->o = L->o.w;
+        d->o_s = L->o.s;
+        d->gu = L->gu.w;
+        d->gu_s = L->gu.s;
+        d->dn = L->down.w;
+        d->dn_s = L->down.s;
+        d->in_norm = L->in_norm;
+        d->post_norm = L->post_norm;
+        const int qk = c->has_qk_norm && L->q_norm && L->k_norm;
+        d->q_norm = qk ? L->q_norm : NULL;
+        d->k_norm = qk ? L->k_norm : NULL;
+    }
+    ctx->use_mk = b2_mk_check(p) == 0;
+}
+
+static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {
+    int rc = ctx_alloc(ctx);
+    if (rc) {
+        fail("context allocation", rc);
+        matmul_decoder_destroy(ctx);
+        return NULL;
+    }
+    mk_setup(ctx);
+    ctx->config = ctx->model.cfg;
+    printf("[MatmulDecoder] Ready: %d layers, hidden=%d, heads=%d/%d, ffn=%d, vocab=%d, quant=%d, "
+           "max_seq=%d, arena %.1f MB, decode kernel: %s\n",
+           ctx->config.num_layers, ctx->config.hidden_dim, ctx->config.num_q_heads,
+           ctx->config.num_kv_heads, ctx->config.ffn_dim, ctx->config.vocab_size, ctx->model.quant,
+           ctx->max_seq, ctx->model.arena.size / 1e6, ctx->use_mk ? "persistent" : "graph");
+    return ctx;
+}
+
+MatmulDecoderContext* matmul_decoder_create(const char* model_dir, const MatmulDecoderConfig* config,
+                                            QuantizationType quant_type, int max_seq_len) {
+    if (!model_dir) return NULL;
+    MatmulDecoderConfig cfg;
+    if (config) {
+        cfg = *config;
+    } else {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/config.json", model_dir);
+        if (matmul_decoder_load_config(path, &cfg) != 0) {
+            MD_LOG("Failed to load config from %s\n", path);
+            return NULL;
+        }
+    }
+    if (max_seq_len <= 0) max_seq_len = cfg.max_seq_len > 0 ? cfg.max_seq_len : 4096;
+    MatmulDecoderContext* ctx = ctx_new(&cfg, max_seq_len);
+    if (!ctx) return NULL;
+    int rc = md_model_load_dir(&ctx->model, model_dir, &cfg, quant_type, max_seq_len,
+                               ctx_bytes(&cfg, max_seq_len, ctx->rows_cap, ctx->split_decode));
+    if (rc) {
+        MD_LOG("Failed to create decoder from %s (%d)\n", model_dir, rc);
+        matmul_decoder_destroy(ctx);
+        return NULL;
+    }
+    return ctx_finish(ctx);
+}
+
+MatmulDecoderContext* matmul_decoder_create_from_weights(const MatmulDecoderConfig* config,
+                                                         const float* embeddings,
+                                                         const LayerWeights* layers,
+                                                         const float* lm_head, QuantizationType quant_type,
+                                                         int max_seq_len) {
+    if (!config || !embeddings || !layers) return NULL;
+    if (config->num_lm_heads > 1) {
+        MD_LOG("create_from_weights: multi-head models load from a directory\n");
+        return NULL;
+    }
+    if (max_seq_len <= 0) max_seq_len = config->max_seq_len > 0 ? config->max_seq_len : 4096;
+    HostLayer* hl = (HostLayer*)calloc((size_t)config->num_layers, sizeof(HostLayer));
+    if (!hl) return NULL;
+    for (int l = 0; l < config->num_layers; l++) {
+        const ProjectionWeight* p[7] = {&layers[l].q_proj, &layers[l].k_proj, &layers[l].v_proj,
+                                        &layers[l].o_proj, &layers[l].gate_proj, &layers[l].up_proj,
+                                        &layers[l].down_proj};
+        for (int i = 0; i < 7; i++) {
+            hl[l].w[i] = p[i]->data;
+            hl[l].s[i] = p[i]->scales;
+            hl[l].wt[i] = p[i]->quant_type == QUANT_INT8 ? B2_W_I8
+                          : (p[i]->quant_type == QUANT_INT4 || p[i]->quant_type == QUANT_INT4_G128) ? B2_W_I4
+                                                                                                 : B2_W_F16;
+        }
+        hl[l].in_norm = layers[l].input_norm_weight;
+        hl[l].post_norm = layers[l].post_attn_norm_weight;
+        hl[l].q_norm = layers[l].q_norm_weight;
+        hl[l].k_norm = layers[l].k_norm_weight;
+    }
+    MatmulDecoderContext* ctx = ctx_new(config, max_seq_len);
+    int rc = ctx ? md_model_from_host(&ctx->model, config, quant_type, max_seq_len, embeddings,
+                                      config->tie_word_embeddings ? NULL : lm_head, hl,
+                                      ctx_bytes(config, max_seq_len, ctx->rows_cap, ctx->split_decode))
+                 : MATMUL_DECODER_ERR_MEMORY;
+    free(hl);
+    if (rc) {
+        MD_LOG("create_from_weights failed (%d)\n", rc);
+        matmul_decoder_destroy(ctx);
+        return NULL;
+    }
+    return ctx_finish(ctx);
+}
+
+void matmul_decoder_destroy(MatmulDecoderContext* ctx) {
+    if (!ctx) return;
+    b2_set_device(ctx->device);
+    if (ctx->stream) b2_stream_sync(ctx->stream);
+    b2_graph_destroy(ctx->g_head);
+    b2_graph_destroy(ctx->g_nohead);
+    b2_graph_destroy(ctx->g_loop);
+    for (int i = 0; i < 3; i++) b2_event_destroy(ctx->ev[i]);
+    b2_stream_destroy(ctx->stream);
+    b2_host_free(ctx->h_blk);
+    b2_host_free(ctx->h_tok);
+    b2_host_free(ctx->h_pos);
+    b2_host_free(ctx->h_loop);
+    b2_host_free(ctx->h_mk_state);
+    md_model_free(&ctx->model);
+    free(ctx);
+}
+
+/* ─── the decode step ─── */
+
+static B2KVRef kv_ref(const MatmulDecoderContext* ctx, const int* pos) {
+    B2KVRef kv;
+    kv.k_base = ctx->k_cache;
+    kv.v_base = ctx->v_cache;
+    kv.seq_stride = 0;
+    kv.layer_stride = ctx->layer_stride;
+    kv.layer = 0;
+    kv.max_seq = ctx->max_seq;
+    kv.rows_seq = NULL;
+    kv.pos = pos;
+    kv.n_seqs = 1;
+    return kv;
+}
+
+/* Kernels of one token: embed, layers, and (head != NULL) lm_head + argmax
+ * with the given table.  Shared by graph capture and the uncaptured path. */
+static int enqueue_token(MatmulDecoderContext* ctx, int with_head, const void* table, const float* scales,
+                         int wtype, int vocab, int copy_params) {
+    DevModel* m = &ctx->model;
+    const int H = m->cfg.hidden_dim;
+    b2_stream_t s = ctx->stream;
+    int rc = 0;
+    if (copy_params) rc = b2_memcpy_h2d(ctx->d_blk, ctx->h_blk, (PARAMS_INTS + H) * 4, s);
+    if (!rc) rc = b2_event_record(ctx->ev[0], s);
+    if (!rc)
+        rc = b2_embed(ctx->hidden, m->emb, ctx->d_blk, ctx->d_blk + 1, (const float*)(ctx->d_blk + PARAMS_INTS),
+                      1, H, s);
+    B2KVRef kv = kv_ref(ctx, ctx->d_blk + 4);
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode};
+    if (!rc) rc = md_enqueue_layers(m, &lb, 1, &kv, s);
+    if (!rc) rc = b2_event_record(ctx->ev[1], s);
+    if (!rc && with_head) {
+        rc = b2_lm_head_argmax(ctx->hidden, H, 1, H, vocab, table, scales, wtype, m->final_norm,
+                               m->cfg.rms_eps, ctx->logits, vocab, ctx->d_tok, ctx->lm_work, s);
+        if (!rc) rc = b2_memcpy_d2h(ctx->h_tok, ctx->d_tok, 4, s);
+    }
+    if (!rc) rc = b2_event_record(ctx->ev[2], s);
+    return rc;
+}
+
+static int build_graph(MatmulDecoderContext* ctx, int with_head, b2_graph_t* g) {
+    int rc = b2_graph_begin(ctx->stream);
+    if (rc) return rc;
+    DevModel* m = &ctx->model;
+    int rc2 = enqueue_token(ctx, with_head, m->lm, m->lm_scales, m->lm_wtype, m->cfg.vocab_size, 1);
+    b2_graph_t tmp = NULL;
+    rc = b2_graph_end(ctx->stream, &tmp);
+    if (rc2) {
+        b2_graph_destroy(tmp);
+        return rc2;
+    }
+    if (rc) return rc;
+    *g = tmp;
+    return 0;
+}
+
+static int check_step_args(MatmulDecoderContext* ctx, int token_id, const float* embedding, int vocab) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (!embedding && (token_id < 0 || token_id >= vocab)) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (ctx->seq_len >= ctx->max_seq) {
+        MD_LOG("KV cache full: seq_len=%d >= max=%d\n", ctx->seq_len, ctx->max_seq);
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    }
+    return 0;
+}
+
+static void stage_params(MatmulDecoderContext* ctx, int token_id, const float* embedding) {
+    const int H = ctx->model.cfg.hidden_dim;
+    ctx->h_blk[0] = embedding ? 0 : token_id;
+    ctx->h_blk[1] = embedding ? 1 : 0;
+    ctx->h_blk[4] = ctx->seq_len;
+    if (embedding) memcpy(ctx->h_blk + PARAMS_INTS, embedding, (size_t)H * 4);
+}
+
+static void record_stats(MatmulDecoderContext* ctx, double t0, double t_copy, int with_head) {
+    float layers_ms = 0.f, head_ms = 0.f;
+    b2_event_elapsed_ms(&layers_ms, ctx->ev[0], ctx->ev[1]);
+    if (with_head) b2_event_elapsed_ms(&head_ms, ctx->ev[1], ctx->ev[2]);
+    ctx->stats.total_ms = (float)(now_ms() - t0);
+    ctx->stats.matmul_ms = layers_ms;
+    ctx->stats.rebind_ms = 0.f;
+    ctx->stats.convert_ms = (float)t_copy;
+    ctx->stats.cpu_ops_ms = 0.f;
+    ctx->stats.lm_head_ms = head_ms;
+    ctx->stats.n_steps++;
+}
+
+/* A persistent-kernel wait timed out: clear its counters and generation so the
+ * next step starts from a consistent state, and report a runtime error. */
+static int mk_recover(MatmulDecoderContext* ctx, int code) {
+    MD_LOG("persistent decode kernel reported error %d (timed-out wait); state reset\n", code);
+    const MatmulDecoderConfig* c = &ctx->model.cfg;
+    const size_t bytes = b2_mk_scratch_bytes(c->num_layers, c->hidden_dim, c->ffn_dim, c->num_q_heads,
+                                             c->num_kv_heads, c->head_dim);
+    b2_memset(ctx->mk_scratch, 0, bytes, ctx->stream);
+    b2_memset(ctx->d_mk_state, 0, B2_MK_STATE_INTS * 4, ctx->stream);
+    b2_stream_sync(ctx->stream);
+    return MATMUL_DECODER_ERR_RKNN;
+}
+
+static int mk_step(MatmulDecoderContext* ctx, int token_id, const float* embedding, int with_head,
+                   float* logits_out) {
+    const double t0 = now_ms();
+    const int H = ctx->model.cfg.hidden_dim;
+    int* st = ctx->h_mk_state;
+    st[B2_MK_TOKEN] = embedding ? 0 : token_id;
+    st[B2_MK_POS] = ctx->seq_len;
+    st[B2_MK_STEP] = 0;
+    st[B2_MK_USE_EMB] = embedding ? 1 : 0;
+    b2_stream_t s = ctx->stream;
+    int rc = b2_memcpy_h2d(ctx->d_mk_state, st, 4 * 4, s);
+    if (!rc && embedding) {
+        memcpy(ctx->h_blk + PARAMS_INTS, embedding, (size_t)H * 4);
+        rc = b2_memcpy_h2d(ctx->d_blk + PARAMS_INTS, ctx->h_blk + PARAMS_INTS, (size_t)H * 4, s);
+    }
+    ctx->mk.do_lm = with_head;
+    if (!rc) rc = b2_event_record(ctx->ev[0], s);
+    if (!rc) rc = b2_mk_decode(&ctx->mk, s);
+    if (!rc) rc = b2_event_record(ctx->ev[2], s);
+    if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, ctx->d_mk_state + B2_MK_ERR, 2 * 4, s);
+    if (!rc) rc = b2_stream_sync(s);
+    if (rc) return fail("persistent decode step", rc);
+    if (st[B2_MK_ERR]) return mk_recover(ctx, st[B2_MK_ERR]);
+    double t_copy = 0;
+    if (with_head && logits_out) {
+        const double tc = now_ms();
+        if ((rc = b2_memcpy_d2h(logits_out, ctx->logits, (size_t)ctx->model.cfg.vocab_size * 4, s)) ||
+            (rc = b2_stream_sync(s)))
+            return fail("logits copy", rc);
+        t_copy = now_ms() - tc;
+    }
+    ctx->seq_len++;
+    ctx->hidden_mk = 1;
+    float ms = 0.f;
+    b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[2]);
+    ctx->stats.total_ms = (float)(now_ms() - t0);
+    ctx->stats.matmul_ms = ms;
+    ctx->stats.rebind_ms = 0.f;
+    ctx->stats.convert_ms = (float)t_copy;
+    ctx->stats.cpu_ops_ms = 0.f;
+    ctx->stats.lm_head_ms = 0.f;
+    ctx->stats.n_steps++;
+    return with_head ? st[B2_MK_TOKEN_OUT] : 0;
+}
+
+/* with_head: run final norm + lm_head + argmax; logits_out: optional host copy. */
+static int step_impl(MatmulDecoderContext* ctx, int token_id, const float* embedding, int with_head,
+                     float* logits_out) {
+    int rc = check_step_args(ctx, token_id, embedding, ctx ? ctx->model.cfg.vocab_size : 0);
+    if (rc) return rc;
+    b2_set_device(ctx->device);
+    if (ctx->use_mk) return mk_step(ctx, token_id, embedding, with_head, logits_out);
+    const double t0 = now_ms();
+    b2_graph_t* g = with_head ? &ctx->g_head : &ctx->g_nohead;
+    if (!*g && (rc = build_graph(ctx, with_head, g))) return fail("graph capture", rc);
+    stage_params(ctx, token_id, embedding);
+    if ((rc = b2_graph_launch(*g, ctx->stream)) || (rc = b2_stream_sync(ctx->stream)))
+        return fail("decode step", rc);
+    double t_copy = 0;
+    if (with_head && logits_out) {
+        const double tc = now_ms();
+        if ((rc = b2_memcpy_d2h(logits_out, ctx->logits, (size_t)ctx->model.cfg.vocab_size * 4, ctx->stream)) ||
+            (rc = b2_stream_sync(ctx->stream)))
+            return fail("logits copy", rc);
+        t_copy = now_ms() - tc;
+    }
+    ctx->seq_len++;
+    ctx->hidden_row = 0;
+    ctx->hidden_mk = 0;
+    record_stats(ctx, t0, t_copy, with_head);
+    return with_head ? ctx->h_tok[0] : 0;
+}
+
+int matmul_decoder_step(MatmulDecoderContext* ctx, int token_id, const float* embedding,
+                        float* output_logits) {
+    /* NULL logits = prefill mode (src/matmul_decoder.c:1551-1561). */
+    return step_impl(ctx, token_id, embedding, output_logits != NULL, output_logits);
+}
+
+int matmul_decoder_step_get_logits(MatmulDecoderContext* ctx, int token_id, const float* embedding,
+                                   float* logits_out) {
+    if (!logits_out) return MATMUL_DECODER_ERR_INVALID_ARG;
+    return step_impl(ctx, token_id, embedding, 1, logits_out);
+}
+
+int matmul_decoder_step_token(MatmulDecoderContext* ctx, int token_id, const float* embedding) {
+    return step_impl(ctx, token_id, embedding, 1, NULL);
+}
+
+int matmul_decoder_step_head(MatmulDecoderContext* ctx, int token_id, const float* embedding,
+                             int lm_head_idx, float* output_logits) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    DevModel* m = &ctx->model;
+    if (m->n_lm_heads <= 1) return matmul_decoder_step(ctx, token_id, embedding, output_logits);
+    if (lm_head_idx < 0 || lm_head_idx >= m->n_lm_heads) return MATMUL_DECODER_ERR_INVALID_ARG;
+    int rc = check_step_args(ctx, token_id, embedding, m->cfg.vocab_size);
+    if (rc) return rc;
+    const double t0 = now_ms();
+    b2_set_device(ctx->device);
+    stage_params(ctx, token_id, embedding);
+    /* Multi-head steps run uncaptured: the table differs per call. */
+    rc = enqueue_token(ctx, 1, m->lm_heads[lm_head_idx], NULL, B2_W_F32, m->lm_vocab, 1);
+    if (!rc) rc = b2_stream_sync(ctx->stream);
+    if (rc) return fail("step_head", rc);
+    double t_copy = 0;
+    if (output_logits) {
+        const double tc = now_ms();
+        if ((rc = b2_memcpy_d2h(output_logits, ctx->logits, (size_t)m->lm_vocab * 4, ctx->stream)) ||
+            (rc = b2_stream_sync(ctx->stream)))
+            return fail("logits copy", rc);
+        t_copy = now_ms() - tc;
+    }
+    ctx->seq_len++;
+    ctx->hidden_row = 0;
+    ctx->hidden_mk = 0;
+    record_stats(ctx, t0, t_copy, 1);
+    return ctx->h_tok[0];
+}
+
+/* ─── device-resident greedy loop ─── */
+
+static int build_loop_graph(MatmulDecoderContext* ctx) {
+    DevModel* m = &ctx->model;
+    const int H = m->cfg.hidden_dim;
+    b2_stream_t s = ctx->stream;
+    int rc = b2_graph_begin(s);
+    if (rc) return rc;
+    int rc2 = b2_embed(ctx->hidden, m->emb, ctx->d_loop, NULL, NULL, 1, H, s);
+    B2KVRef kv = kv_ref(ctx, ctx->d_loop + 1);
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode};
+    if (!rc2) rc2 = md_enqueue_layers(m, &lb, 1, &kv, s);
+    if (!rc2)
+        rc2 = b2_lm_head_argmax(ctx->hidden, H, 1, H, m->cfg.vocab_size, m->lm, m->lm_scales, m->lm_wtype,
+                                m->final_norm, m->cfg.rms_eps, ctx->logits, m->cfg.vocab_size, ctx->d_loop,
+                                ctx->lm_work, s);
+    if (!rc2) rc2 = b2_loop_advance(ctx->d_loop, ctx->d_hist, ctx->max_seq, s);
+    b2_graph_t g = NULL;
+    rc = b2_graph_end(s, &g);
+    if (rc2 || rc) {
+        b2_graph_destroy(g);
+        return rc2 ? rc2 : rc;
+    }
+    ctx->g_loop = g;
+    return 0;
+}
+
+int matmul_decoder_decode_greedy(MatmulDecoderContext* ctx, int first_token, int n_tokens, int* tokens_out,
+                                 float* device_ms) {
+    if (!ctx || !tokens_out || n_tokens <= 0) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (ctx->model.n_lm_heads > 1) return MATMUL_DECODER_ERR_UNSUPPORTED;
+    if (first_token < 0 || first_token >= ctx->model.cfg.vocab_size) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (ctx->seq_len + n_tokens > ctx->max_seq) {
+        MD_LOG("decode_greedy: seq_len=%d + %d > max=%d\n", ctx->seq_len, n_tokens, ctx->max_seq);
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    }
+    const double t0 = now_ms();
+    b2_set_device(ctx->device);
+    int rc = 0;
+    if (ctx->use_mk) {
+        int* st = ctx->h_mk_state;
+        st[B2_MK_TOKEN] = first_token;
+        st[B2_MK_POS] = ctx->seq_len;
+        st[B2_MK_STEP] = 0;
+        st[B2_MK_USE_EMB] = 0;
+        ctx->mk.do_lm = 1;
+        rc = b2_memcpy_h2d(ctx->d_mk_state, st, 4 * 4, ctx->stream);
+        if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
+        for (int i = 0; i < n_tokens && !rc; i++) rc = b2_mk_decode(&ctx->mk, ctx->stream);
+        if (!rc) rc = b2_event_record(ctx->ev[2], ctx->stream);
+        if (!rc) rc = b2_memcpy_d2h(tokens_out, ctx->d_hist, (size_t)n_tokens * 4, ctx->stream);
+        if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, ctx->d_mk_state + B2_MK_ERR, 4, ctx->stream);
+        if (!rc) rc = b2_stream_sync(ctx->stream);
+        if (rc) return fail("decode_greedy", rc);
+        if (st[B2_MK_ERR]) return mk_recover(ctx, st[B2_MK_ERR]);
+        float ms = 0.f;
+        b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[2]);
+        if (device_ms) *device_ms = ms;
+        ctx->seq_len += n_tokens;
+        ctx->hidden_mk = 1;
+        ctx->stats.total_ms = (float)(now_ms() - t0);
+        ctx->stats.matmul_ms = ms;
+        ctx->stats.lm_head_ms = 0.f;
+        ctx->stats.n_steps += n_tokens;
+        return n_tokens;
+    }
+    if (!ctx->g_loop && (rc = build_loop_graph(ctx))) return fail("loop graph capture", rc);
+    ctx->h_loop[0] = first_token;
+    ctx->h_loop[1] = ctx->seq_len;
+    ctx->h_loop[2] = 0;
+    ctx->h_loop[3] = 0;
+    rc = b2_memcpy_h2d(ctx->d_loop, ctx->h_loop, 16, ctx->stream);
+    if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
+    for (int i = 0; i < n_tokens && !rc; i++) rc = b2_graph_launch(ctx->g_loop, ctx->stream);
+    if (!rc) rc = b2_event_record(ctx->ev[2], ctx->stream);
+    if (!rc) rc = b2_memcpy_d2h(tokens_out, ctx->d_hist, (size_t)n_tokens * 4, ctx->stream);
+    if (!rc) rc = b2_stream_sync(ctx->stream);
+    if (rc) return fail("decode_greedy", rc);
+    float ms = 0.f;
+    b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[2]);
+    if (device_ms) *device_ms = ms;
+    ctx->seq_len += n_tokens;
+    ctx->hidden_row = 0;
+    ctx->hidden_mk = 0;
+    ctx->stats.total_ms = (float)(now_ms() - t0);
+    ctx->stats.matmul_ms = ms;
+    ctx->stats.lm_head_ms = 0.f;
+    ctx->stats.n_steps += n_tokens;
+    return n_tokens;
+}
+
+/* ─── batch prefill ─── */
+
+int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddings, int M) {
+    if (!ctx || !embeddings || M <= 0) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (ctx->seq_len + M > ctx->max_seq) {
+        fprintf(stderr, "[BatchPrefill] KV cache overflow: seq_len=%d + M=%d > max=%d\n", ctx->seq_len, M,
+                ctx->max_seq);
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    }
+    b2_set_device(ctx->device);
+    DevModel* m = &ctx->model;
+    const int H = m->cfg.hidden_dim;
+    for (int off = 0; off < M; off += ctx->rows_cap) {
+        const int rows = M - off < ctx->rows_cap ? M - off : ctx->rows_cap;
+        for (int i = 0; i < rows; i++) ctx->h_pos[i] = ctx->seq_len + i;
+        int rc = b2_memcpy_h2d(ctx->hidden, embeddings + (size_t)off * H, (size_t)rows * H * 4, ctx->stream);
+        if (!rc) rc = b2_memcpy_h2d(ctx->d_pos, ctx->h_pos, (size_t)rows * 4, ctx->stream);
+        B2KVRef kv = kv_ref(ctx, ctx->d_pos);
+        int split = (296 + rows * m->cfg.num_kv_heads - 1) / (rows * m->cfg.num_kv_heads);
+        if (split < 1) split = 1;
+        if (split > ctx->split_decode) split = ctx->split_decode;
+        LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, split};
+        if (!rc) rc = md_enqueue_layers(m, &lb, rows, &kv, ctx->stream);
+        if (!rc) rc = b2_stream_sync(ctx->stream);
+        if (rc) return fail("prefill_batch", rc);
+        ctx->seq_len += rows;
+        ctx->hidden_row = rows - 1;
+        ctx->hidden_mk = 0;
+    }
+    return MATMUL_DECODER_OK;
+}
+
+/* ─── state queries ─── */
+
+void matmul_decoder_clear_kv_cache(MatmulDecoderContext* ctx) {
+    if (ctx) ctx->seq_len = 0;
+}
+
+int matmul_decoder_get_seq_len(const MatmulDecoderContext* ctx) { return ctx ? ctx->seq_len : 0; }
+
+const MatmulDecoderConfig* matmul_decoder_get_config(const MatmulDecoderContext* ctx) {
+    return ctx ? &ctx->config : NULL;
+}
+
+void matmul_decoder_get_stats(const MatmulDecoderContext* ctx, MatmulDecoderStats* stats) {
+    if (ctx && stats) *stats = ctx->stats;
+}
+
+int matmul_decoder_set_seq_len(MatmulDecoderContext* ctx, int n) {
+    if (!ctx || n < 0 || n > ctx->max_seq) return MATMUL_DECODER_ERR_INVALID_ARG;
+    ctx->seq_len = n;
+    return MATMUL_DECODER_OK;
+}
+
+int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out) {
+    if (!ctx || !hidden_out) return MATMUL_DECODER_ERR_INVALID_ARG;
+    b2_set_device(ctx->device);
+    const size_t H = (size_t)ctx->model.cfg.hidden_dim;
+    const float* src = ctx->hidden_mk ? b2_mk_final_hidden(&ctx->mk) : ctx->hidden + (size_t)ctx->hidden_row * H;
+    int rc = b2_memcpy_d2h(hidden_out, src, H * 4, ctx->stream);
+    if (!rc) rc = b2_stream_sync(ctx->stream);
+    return rc ? fail("get_hidden", rc) : MATMUL_DECODER_OK;
+}
+
+/* Host [len][nkv][hd] <-> device [nkv][max_seq][hd] for one layer. */
+static int kv_transfer(MatmulDecoderContext* ctx, int layer, int start, int len, uint16_t* kh, uint16_t* vh,
+                       int to_device) {
+    const MatmulDecoderConfig* c = &ctx->model.cfg;
+    if (layer < 0 || layer >= c->num_layers || start < 0 || len <= 0 || start + len > ctx->max_seq || !kh ||
+        !vh)
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    b2_set_device(ctx->device);
+    const int nkv = c->num_kv_heads, hd = c->head_dim;
+    uint16_t* tmp = (uint16_t*)malloc((size_t)len * nkv * hd * 2);
+    if (!tmp) return MATMUL_DECODER_ERR_MEMORY;
+    int rc = 0;
+    for (int which = 0; which < 2 && !rc; which++) {
+        uint16_t* host = which ? vh : kh;
+        uint16_t* dev = (which ? ctx->v_cache : ctx->k_cache) + (size_t)layer * ctx->layer_stride;
+        if (to_device)
+            for (int g = 0; g < nkv; g++)
+                for (int p = 0; p < len; p++)
+                    memcpy(tmp + ((size_t)g * len + p) * hd, host + ((size_t)p * nkv + g) * hd, (size_t)hd * 2);
+        for (int g = 0; g < nkv && !rc; g++) {
+            uint16_t* d = dev + ((size_t)g * ctx->max_seq + start) * hd;
+            rc = to_device ? b2_memcpy_h2d(d, tmp + (size_t)g * len * hd, (size_t)len * hd * 2, ctx->stream)
+                           : b2_memcpy_d2h(tmp + (size_t)g * len * hd, d, (size_t)len * hd * 2, ctx->stream);
+        }
+        if (!rc) rc = b2_stream_sync(ctx->stream);
+        if (!rc && !to_device)
+            for (int g = 0; g < nkv; g++)
+                for (int p = 0; p < len; p++)
+                    memcpy(host + ((size_t)p * nkv + g) * hd, tmp + ((size_t)g * len + p) * hd, (size_t)hd * 2);
+    }
+    free(tmp);
+    return rc ? fail("kv transfer", rc) : MATMUL_DECODER_OK;
+}
+
+int matmul_decoder_set_kv(MatmulDecoderContext* ctx, int layer, int start, int len, const uint16_t* k_fp16,
+                          const uint16_t* v_fp16) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    return kv_transfer(ctx, layer, start, len, (uint16_t*)k_fp16, (uint16_t*)v_fp16, 1);
+}
+
+int matmul_decoder_get_kv(MatmulDecoderContext* ctx, int layer, int start, int len, uint16_t* k_fp16,
+                          uint16_t* v_fp16) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    return kv_transfer(ctx, layer, start, len, k_fp16, v_fp16, 0);
+}

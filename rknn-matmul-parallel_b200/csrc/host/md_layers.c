@@ -1,0 +1,56 @@
+/*
+ * One pass of M rows through every layer, as a sequence of fused kernels on
+ * one stream (captured into a CUDA graph by the callers).
+ *
+ * Per layer this is the body of matmul_decoder_step / prefill_batch
+ * (src/matmul_decoder.c:1464-1546, :1970-2061) regrouped into five kernels
+ * plus the attention combine:
+ *   1. RMSNorm(input_norm) + fused q|k|v GEMV                       (b2_gemv)
+ *   2. per-head q/k RMSNorm + RoPE + K/V store at pos              (b2_qk_rope_kv)
+ *   3. GQA attention over [0, pos] (split-KV + combine)            (b2_attention)
+ *   4. o_proj GEMV + residual add into hidden                       (b2_gemv ADD)
+ *   5. RMSNorm(post_attn_norm) + gate|up GEMV + SiLU*mul            (b2_gemv SILU_PAIR)
+ *   6. down GEMV + residual add into hidden                         (b2_gemv ADD)
+ * K/V of the current rows are stored before attention for decode and
+ * prefill alike; the reference stores them after attention in prefill
+ * (:2026-2034) but reads the same values from its batch buffers, so the
+ * attended set is identical.
+ */
+#include <stdio.h>
+
+#include "md_internal.h"
+
+int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2KVRef* kv_proto,
+                      b2_stream_t s) {
+    const MatmulDecoderConfig* c = &m->cfg;
+    const int H = c->hidden_dim, hd = c->head_dim, nq = c->num_q_heads, nkv = c->num_kv_heads;
+    const int qd = nq * hd, kvd = nkv * hd, F = c->ffn_dim, ldqkv = qd + 2 * kvd;
+    for (int l = 0; l < c->num_layers; l++) {
+        const DevLayer* L = &m->layers[l];
+        B2GemvArgs a = {b->qkv, ldqkv, b->hidden, H, M, H, ldqkv, L->qkv.w, L->qkv.s, L->qkv.wtype,
+                        L->in_norm, c->rms_eps, B2_EPI_STORE};
+        int rc = b2_gemv(&a, s);
+        if (rc) return rc;
+        B2KVRef kv = *kv_proto;
+        kv.layer = l;
+        const int qk = c->has_qk_norm && L->q_norm && L->k_norm;
+        rc = b2_qk_rope_kv(b->qkv, ldqkv, M, nq, nkv, hd, qk ? L->q_norm : NULL, qk ? L->k_norm : NULL,
+                           c->rms_eps, m->cos_tab, m->sin_tab, c->rope_style, &kv, s);
+        if (rc) return rc;
+        rc = b2_attention(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
+        if (rc) return rc;
+        B2GemvArgs o = {b->hidden, H, b->attn, qd, M, qd, H, L->o.w, L->o.s, L->o.wtype, NULL, 0.f,
+                        B2_EPI_ADD};
+        rc = b2_gemv(&o, s);
+        if (rc) return rc;
+        B2GemvArgs gu = {b->act, F, b->hidden, H, M, H, F, L->gu.w, L->gu.s, L->gu.wtype, L->post_norm,
+                         c->rms_eps, B2_EPI_SILU_PAIR};
+        rc = b2_gemv(&gu, s);
+        if (rc) return rc;
+        B2GemvArgs dn = {b->hidden, H, b->act, F, M, F, H, L->down.w, L->down.s, L->down.wtype, NULL, 0.f,
+                         B2_EPI_ADD};
+        rc = b2_gemv(&dn, s);
+        if (rc) return rc;
+    }
+    return 0;
+}
