@@ -217,7 +217,8 @@ typedef struct {
     int hist_len;
     int do_lm;                 /* 0 = prefill-mode step (no final norm/lm_head) */
     void* scratch;             /* b2_mk_scratch_bytes() bytes, zeroed once    */
-    B2MkLayer layer[B2_MK_MAX_LAYERS];
+    const B2MkLayer* layers;   /* device array [n_layers] (kept off the kernel
+                                  parameter block, which stays small)         */
 } B2MkPlan;
 
 /* 0 when the plan's shapes are supported by the persistent kernel. */

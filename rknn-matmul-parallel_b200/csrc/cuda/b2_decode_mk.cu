@@ -255,7 +255,7 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
     const int cap_h = kStageBytes / (int)rb_h, cap_q = kStageBytes / (int)rb_q, cap_f = kStageBytes / (int)rb_f;
     const int cap_pair = kStageBytes / (2 * (int)rb_h);
     for (int l = 0; l < p.n_layers; l++) {
-        const B2MkLayer& Lw = p.layer[l];
+        const B2MkLayer& Lw = p.layers[l];
         if (v.stop()) return;
         {  // q|k|v rows
             Item it{IT_QKV, l, split_lo(geo.nqkv, geo.G, geo.cta), split_lo(geo.nqkv, geo.G, geo.cta + 1), 0, 0, 0, 0};
@@ -349,8 +349,8 @@ struct Shared {
     unsigned long long best[kCWarps];
     float q[kMaxGq][kHD];                  // normalized + rotated q heads of the group
     float k[kHD], v[kHD];                  // new k (rotated) and v of the kv head
-    float gm[16][kMaxGq], gl[16][kMaxGq];  // per lane-group softmax state
-    float go[16][kMaxGq][kHD];             // per lane-group partial outputs
+    float gm[kCWarps][kMaxGq], gl[kCWarps][kMaxGq];  // per-warp softmax state
+    float go[kCWarps][kMaxGq][kHD];                   // per-warp partial outputs
 };
 
 __device__ __forceinline__ void set_error(const B2MkPlan& p, Shared& sh, int code) {
@@ -486,7 +486,7 @@ struct Consumer {
         switch (it.type) {
             case IT_QKV:
                 if (it.l > 0) wait_counter(cnt(it.l - 1, C_DN), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(hidden_in(it.l), H, p.layer[it.l].in_norm);
+                if (!stop()) stage_x(hidden_in(it.l), H, p.layers[it.l].in_norm);
                 break;
             case IT_ATTN: {
                 wait_counter(cnt(it.l, C_QKV + it.g), (unsigned long long)(geo.Gq + 2) * kHD * target);
@@ -500,7 +500,7 @@ struct Consumer {
                 break;
             case IT_GU:
                 wait_counter(cnt(it.l, C_O), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(S.hmid + (size_t)it.l * H, H, p.layer[it.l].post_norm);
+                if (!stop()) stage_x(S.hmid + (size_t)it.l * H, H, p.layers[it.l].post_norm);
                 break;
             case IT_DN:
                 wait_counter(cnt(it.l, C_GU), (unsigned long long)geo.G * target);
@@ -541,9 +541,9 @@ struct Consumer {
         switch (c.type) {
             case IT_QKV: rows_qkv(c, buf); break;
             case IT_ATTN: attn_chunk(c, buf); break;
-            case IT_O: rows_resid(c, buf, geo.qd, p.layer[c.l].o, p.layer[c.l].o_s, S.hmid); break;
+            case IT_O: rows_resid(c, buf, geo.qd, p.layers[c.l].o, p.layers[c.l].o_s, S.hmid); break;
             case IT_GU: rows_gu(c, buf); break;
-            case IT_DN: rows_resid(c, buf, p.ffn, p.layer[c.l].dn, p.layer[c.l].dn_s, S.hbuf); break;
+            case IT_DN: rows_resid(c, buf, p.ffn, p.layers[c.l].dn, p.layers[c.l].dn_s, S.hbuf); break;
             case IT_LM: rows_lm(c, buf); break;
         }
         consumer_sync();  // every consumer is done reading the stage
@@ -602,7 +602,7 @@ struct Consumer {
 
     __device__ void rows_qkv(const Chunk& c, const unsigned char* buf) {
         const size_t rb = row_bytes(WT, p.hidden);
-        const float* sc = p.layer[c.l].qkv_s;
+        const float* sc = p.layers[c.l].qkv_s;
         float* out = S.qkv + (size_t)c.l * geo.nqkv;
         for (int r = c.a + warp; r < c.b; r += kCWarps) {
             const float d = row_dot<WT>(buf + (size_t)(r - c.a) * rb, xs, p.hidden, lane);
@@ -629,7 +629,7 @@ struct Consumer {
 
     __device__ void rows_gu(const Chunk& c, const unsigned char* buf) {
         const size_t rb = row_bytes(WT, p.hidden);
-        const float* sc = p.layer[c.l].gu_s;
+        const float* sc = p.layers[c.l].gu_s;
         float* act = S.act + (size_t)c.l * p.ffn;
         const int n = c.b - c.a;
         for (int j = warp; j < n; j += kCWarps) {
@@ -661,7 +661,7 @@ struct Consumer {
     __device__ void attn_prologue(const Item& it) {
         const int Gq = geo.Gq;
         const float* qkv = S.qkv + (size_t)it.l * geo.nqkv;
-        const B2MkLayer& Lw = p.layer[it.l];
+        const B2MkLayer& Lw = p.layers[it.l];
         const int h = warp;  // warps 0..Gq-1: q heads, Gq: k head, Gq+1: v head
         if (h <= Gq + 1) {
             const int e0 = lane * 4;
@@ -697,7 +697,9 @@ struct Consumer {
                     for (int j = 0; j < 4; j++) {
                         const float other = __shfl_xor_sync(0xffffffffu, x[j], 16);
                         const int e = e0 + j;
-                        x[j] = lane < 16 ? x[j] * cs[e] - other * sn[e] : x[j] * cs[e - 64] + other * sn[e - 64];
+                        const int i = lane < 16 ? e : e - kHD / 2;
+                        const float c0 = cs[i], s0 = sn[i];
+                        x[j] = lane < 16 ? x[j] * c0 - other * s0 : x[j] * c0 + other * s0;
                     }
                 }
             }
@@ -783,7 +785,7 @@ struct Consumer {
     }
 
     __device__ void attn_epilogue(const Item& it) {
-        const int Gq = geo.Gq, sub = lane & 7, grp = warp * 4 + (lane >> 3);
+        const int Gq = geo.Gq, sub = lane & 7;
         // the newest position (not in the cache stream): lane group 0 of warp 0
         if (it.p1 == geo.L && it.p0 <= geo.L - 1 && warp == 0) {
             float kf[16], vf[16];
@@ -795,26 +797,46 @@ struct Consumer {
             }
             attn_update(live, kf, vf);
         }
+        // Merge the four lane groups of this warp (lanes sub, sub^8, sub^16,
+        // sub^24 hold the same 16 dims) with shuffles, then publish one state
+        // per warp.
 #pragma unroll
         for (int h = 0; h < kMaxGq; h++) {
             if (h >= Gq) break;
-            if (sub == 0) {
-                sh.gm[grp][h] = m_[h];
-                sh.gl[grp][h] = l_[h];
-            }
 #pragma unroll
-            for (int j = 0; j < 16; j++) sh.go[grp][h][sub * 16 + j] = o_[h][j];
+            for (int off = 8; off <= 16; off <<= 1) {
+                const float mo = __shfl_xor_sync(0xffffffffu, m_[h], off);
+                const float lo = __shfl_xor_sync(0xffffffffu, l_[h], off);
+                const float M = fmaxf(m_[h], mo);
+                const float a = (m_[h] == -INFINITY) ? 0.f : expf(m_[h] - M);
+                const float b = (mo == -INFINITY) ? 0.f : expf(mo - M);
+                l_[h] = l_[h] * a + lo * b;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float oo = __shfl_xor_sync(0xffffffffu, o_[h][j], off);
+                    o_[h][j] = o_[h][j] * a + oo * b;
+                }
+                m_[h] = M;
+            }
+            if (lane < 8) {
+                if (sub == 0) {
+                    sh.gm[warp][h] = m_[h];
+                    sh.gl[warp][h] = l_[h];
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++) sh.go[warp][h][sub * 16 + j] = o_[h][j];
+            }
         }
         consumer_sync();
-        // merge the 16 lane groups into this unit's partial (thread = (head, dim))
+        // merge the per-warp states into this unit's partial (thread = (head, dim))
         const size_t unit = (((size_t)it.l * p.nkv + it.g) * kMaxSplit + it.s) * Gq;
         for (int t = tid; t < Gq * kHD; t += kConsumers) {
             const int h = t / kHD, d = t % kHD;
             float M = -INFINITY;
-            for (int r = 0; r < 16; r++) M = fmaxf(M, sh.gm[r][h]);
+            for (int r = 0; r < kCWarps; r++) M = fmaxf(M, sh.gm[r][h]);
             float ls = 0.f, acc = 0.f;
             if (M != -INFINITY)
-                for (int r = 0; r < 16; r++) {
+                for (int r = 0; r < kCWarps; r++) {
                     if (sh.gm[r][h] == -INFINITY) continue;
                     const float w = expf(sh.gm[r][h] - M);
                     ls = fmaf(sh.gl[r][h], w, ls);
@@ -1014,7 +1036,7 @@ extern "C" int b2_mk_check(const B2MkPlan* p) {
         row_bytes(p->wtype, p->nq * kHD) > (size_t)kStageBytes || (size_t)p->hidden > (size_t)kStageBytes)
         return B2_ERR_INVALID_ARG;
     if (p->do_lm && (!p->lm || !p->lm_s || !p->final_norm)) return B2_ERR_INVALID_ARG;
-    if (!p->state || !p->scratch || !p->k_cache || !p->v_cache || !p->cos_tab || !p->sin_tab || !p->emb)
+    if (!p->layers || !p->state || !p->scratch || !p->k_cache || !p->v_cache || !p->cos_tab || !p->sin_tab || !p->emb)
         return B2_ERR_INVALID_ARG;
     return 0;
 }

@@ -12,12 +12,12 @@
  * serves every position.  Logits cross to the host only when the caller
  * passes a logits buffer.
  *
- * When the shapes allow it (INT8 lm_head, GQA group <= 2, head_dim 128), a
+ * With B2_DECODE_KERNEL=persistent in the environment at create time, and
+ * when the shapes allow it (INT8 lm_head, GQA group <= 2, head_dim 128), a
  * single-token step runs instead as ONE launch of the persistent decode
  * kernel (b2_mk_decode), which streams the whole token's weights from one
- * CTA per SM.  B2_DECODE_KERNEL=graph in the environment at create time
- * selects the multi-kernel graph instead.  Batch prefill always uses the
- * multi-kernel pass.
+ * CTA per SM.  The graph is the default while it is the faster of the two.
+ * Batch prefill always uses the multi-kernel pass.
  */
 #include <stdio.h>
 #include <stdlib.h>
@@ -51,6 +51,7 @@ struct MatmulDecoderContext {
     int use_mk;       /* persistent decode kernel selected */
     int hidden_mk;    /* last token's hidden lives in the persistent kernel's scratch */
     B2MkPlan mk;
+    B2MkLayer* d_mk_layers; /* device copy of the per-layer pointer table */
     int* d_mk_state;  /* B2_MK_STATE_INTS */
     int* h_mk_state;  /* pinned mirror */
     void* mk_scratch;
@@ -84,6 +85,7 @@ static size_t ctx_bytes(const MatmulDecoderConfig* c, int max_seq, int rows_cap,
     t += (aw1 > aw2 ? aw1 : aw2) + b2_lm_head_workspace(1, (int)vmax) + 1024;
     t += 256 + (size_t)max_seq * 4 + 256;
     t += 256 + b2_mk_scratch_bytes(c->num_layers, (int)H, (int)F, c->num_q_heads, c->num_kv_heads, (int)hd) + 256;
+    t += sizeof(B2MkLayer) * (size_t)c->num_layers + 256;
     return t;
 }
 
@@ -116,6 +118,8 @@ static int ctx_alloc(MatmulDecoderContext* ctx) {
     const size_t mk_bytes =
         b2_mk_scratch_bytes(c->num_layers, (int)H, (int)F, c->num_q_heads, c->num_kv_heads, (int)hd);
     ctx->d_mk_state = (int*)md_arena_alloc(&m->arena, B2_MK_STATE_INTS * 4);
+    ctx->d_mk_layers = (B2MkLayer*)md_arena_alloc(&m->arena, sizeof(B2MkLayer) * (size_t)c->num_layers);
+    if (!ctx->d_mk_layers) return MATMUL_DECODER_ERR_MEMORY;
     ctx->mk_scratch = md_arena_alloc(&m->arena, mk_bytes);
     if (!ctx->d_mk_state || !ctx->mk_scratch) return MATMUL_DECODER_ERR_MEMORY;
     if (b2_memset(ctx->d_mk_state, 0, B2_MK_STATE_INTS * 4, NULL) || b2_memset(ctx->mk_scratch, 0, mk_bytes, NULL))
@@ -156,7 +160,7 @@ static void mk_setup(MatmulDecoderContext* ctx) {
     const char* env = getenv("B2_DECODE_KERNEL");
     DevModel* m = &ctx->model;
     const MatmulDecoderConfig* c = &m->cfg;
-    if ((env && strcmp(env, "graph") == 0) || m->n_lm_heads > 1 || m->lm_wtype != B2_W_I8 ||
+    if (!env || strcmp(env, "persistent") != 0 || m->n_lm_heads > 1 || m->lm_wtype != B2_W_I8 ||
         c->num_layers > B2_MK_MAX_LAYERS)
         return;
     B2MkPlan* p = &ctx->mk;
@@ -188,9 +192,11 @@ static void mk_setup(MatmulDecoderContext* ctx) {
     p->hist_len = ctx->max_seq;
     p->do_lm = 1;
     p->scratch = ctx->mk_scratch;
+    B2MkLayer* table = (B2MkLayer*)calloc((size_t)c->num_layers, sizeof(B2MkLayer));
+    if (!table) return;
     for (int l = 0; l < c->num_layers; l++) {
         const DevLayer* L = &m->layers[l];
-        B2MkLayer* d = &p->layer[l];
+        B2MkLayer* d = &table[l];
         d->qkv = L->qkv.w;
         d->qkv_s = L->qkv.s;
         d->o = L->o.w;
@@ -205,7 +211,11 @@ static void mk_setup(MatmulDecoderContext* ctx) {
         d->q_norm = qk ? L->q_norm : NULL;
         d->k_norm = qk ? L->k_norm : NULL;
     }
-    ctx->use_mk = b2_mk_check(p) == 0;
+    int rc = b2_memcpy_h2d(ctx->d_mk_layers, table, sizeof(B2MkLayer) * (size_t)c->num_layers, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    free(table);
+    p->layers = ctx->d_mk_layers;
+    ctx->use_mk = !rc && b2_mk_check(p) == 0;
 }
 
 static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {

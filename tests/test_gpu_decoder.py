@@ -282,7 +282,11 @@ def test_pybind_module_on_gpu(small_models):
 # ── persistent decode kernel vs the multi-kernel graph path ──
 
 def graph_decoder(mdir, quant, **kw):
-    os.environ["B2_DECODE_KERNEL"] = "graph"
+    return bd.Decoder(mdir, quant, **kw)
+
+
+def persistent_decoder(mdir, quant, **kw):
+    os.environ["B2_DECODE_KERNEL"] = "persistent"
     try:
         return bd.Decoder(mdir, quant, **kw)
     finally:
@@ -292,7 +296,7 @@ def graph_decoder(mdir, quant, **kw):
 @pytest.mark.parametrize("quant", ["fp16", "int8", "int4"])
 def test_persistent_kernel_matches_graph_path(small_models, quant):
     mdir = small_models[quant]
-    mk = bd.Decoder(mdir, quant, max_seq_len=96)
+    mk = persistent_decoder(mdir, quant, max_seq_len=96)
     gr = graph_decoder(mdir, quant, max_seq_len=96)
     emb = mf.seeded_hidden(870_000, 9, 1024)
     mk.prefill_batch(emb)
@@ -315,9 +319,21 @@ def test_persistent_kernel_matches_graph_path(small_models, quant):
     assert_parity(v1.astype(np.float32), v2.astype(np.float32), "V cache")
 
 
+def test_decode_greedy_graph_equals_step_loop(small_models):
+    mdir = small_models["fp16"]
+    a = bd.Decoder(mdir, "fp16", max_seq_len=96)
+    b = bd.Decoder(mdir, "fp16", max_seq_len=96)
+    toks, ms = a.decode_greedy(42, 12)
+    ref_toks, t = [], 42
+    for _ in range(12):
+        t = b.step_token(t)
+        ref_toks.append(t)
+    assert toks.tolist() == ref_toks and ms > 0
+
+
 def test_decode_greedy_equals_step_loop(small_models):
     mdir = small_models["int8"]
-    a = bd.Decoder(mdir, "int8", max_seq_len=96)
+    a = persistent_decoder(mdir, "int8", max_seq_len=96)
     b = bd.Decoder(mdir, "int8", max_seq_len=96)
     emb = mf.seeded_hidden(872_000, 5, 1024)
     a.prefill_batch(emb)
@@ -334,7 +350,7 @@ def test_decode_greedy_equals_step_loop(small_models):
 def test_persistent_kernel_long_context(model_cache):
     """Attention split over many position ranges (L = 3000) plus the fresh position."""
     mdir = model(model_cache, "mk_long", "fp16", num_layers=2, vocab_size=4096, name="mk_long")
-    mk = bd.Decoder(mdir, "fp16", max_seq_len=3100)
+    mk = persistent_decoder(mdir, "fp16", max_seq_len=3100)
     gr = graph_decoder(mdir, "fp16", max_seq_len=3100)
     orc = ref.RefDecoder(mdir, "fp16", max_seq_len=3100, nthreads=NTH)
     for layer in range(2):
