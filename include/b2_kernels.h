@@ -155,6 +155,27 @@ int b2_lm_head_argmax(const float* x, int ldx, int M, int K, int V, const void* 
                       const float* scales, int wtype, const float* norm_w, float eps,
                       float* logits, int ldl, int* tokens, void* work, b2_stream_t s);
 
+/* No counterpart in the reference.  b2_lm_head_argmax for callers that cannot
+ * allocate device memory: code running inside a host that owns all HBM in
+ * its own pool, or enqueueing work while another framework captures the
+ * stream into a CUDA graph (cudaMalloc is not capturable and may synchronize
+ * the device).  Same arguments and results as b2_lm_head_argmax without
+ * `work`: the per-CTA argmax keys live in a fixed 1 MiB device array inside
+ * this library (b2_lm_head_noalloc_max_keys() keys), which every device that
+ * loads the library holds until exit.  Sizes with M x ceil(V / rows per CTA)
+ * above that (rows per CTA: 32 int8, 16 F16, 8 F32) are rejected with
+ * ERR_INVALID_ARG.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on one device share its array and it keeps the last
+ * call's contents: calls that may overlap on the GPU (e.g. on two streams of
+ * the same device) race and must be serialized by the caller.  Every key a
+ * call reads is written by the same call, so nothing needs clearing between
+ * calls. */
+size_t b2_lm_head_noalloc_max_keys(void);
+int b2_lm_head_argmax_noalloc(const float* x, int ldx, int M, int K, int V, const void* table,
+                              const float* scales, int wtype, const float* norm_w, float eps,
+                              float* logits, int ldl, int* tokens, b2_stream_t s);
+
 /* Device-side greedy loop bookkeeping, run once per step after the argmax:
  * hist[loop[2]] = loop[0] (the token just produced, which is also the next
  * step's input), then loop[1] (position) and loop[2] (step counter) advance.

@@ -269,3 +269,78 @@ extern "C" int b2_lm_head_argmax(const float* x, int ldx, int M, int K, int V, c
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_argmax_final: %s", cudaGetErrorString(e));
     return 0;
 }
+
+// ─── the same lm_head + argmax for callers that cannot allocate ───
+//
+// Callers embedded in a host that owns all device memory (a serving runtime
+// that pre-reserves HBM in its own pool) or that enqueue work while another
+// framework is capturing the stream into a CUDA graph cannot call cudaMalloc
+// for a workspace: cudaMalloc is not capturable, it can synchronize the
+// device, and the pool may leave nothing outside its arena.  This entry point
+// keeps the per-CTA argmax keys in a file-scope device array instead.
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocKeys = (size_t)1 << 17;  // 131072 keys = 1 MiB per device
+static __device__ __align__(256) unsigned long long g_lm_noalloc_keys[kNoAllocKeys];
+
+constexpr int kMaxDevices = 64;
+unsigned long long* g_noalloc_addr[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device address of g_lm_noalloc_keys on the current device.  In host code the
+// symbol name is only a host-side handle: the address must come from
+// cudaGetSymbolAddress, once per device, with that device current.
+int noalloc_keys(unsigned long long** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return b2_set_error(B2_ERR_INVALID_ARG, "noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_lm_noalloc_keys);
+        if (e != cudaSuccess)
+            return b2_set_error(B2_ERR_CUDA, "noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_addr[dev] = static_cast<unsigned long long*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" size_t b2_lm_head_noalloc_max_keys(void) { return kNoAllocKeys; }
+
+extern "C" int b2_lm_head_argmax_noalloc(const float* x, int ldx, int M, int K, int V, const void* table,
+                                         const float* scales, int wtype, const float* norm_w, float eps,
+                                         float* logits, int ldl, int* tokens, b2_stream_t stream) {
+    if (M <= 0) return 0;
+    if (!x || !table || !tokens || K <= 0 || V <= 0 || K % 16 != 0 || K > 8192)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_lm_head_argmax_noalloc: bad arguments (K=%d V=%d)", K, V);
+    if (wtype != B2_W_I8 && wtype != B2_W_F16 && wtype != B2_W_F32)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_lm_head_argmax_noalloc: wtype %d", wtype);
+    if (wtype == B2_W_I8 && !scales)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_lm_head_argmax_noalloc: int8 needs scales");
+    const int nb = (V + rows_per_cta(wtype) - 1) / rows_per_cta(wtype);
+    if ((size_t)M * (size_t)nb > kNoAllocKeys)
+        return b2_set_error(B2_ERR_INVALID_ARG,
+                            "b2_lm_head_argmax_noalloc: M=%d x %d CTA keys exceeds the fixed scratch of %zu keys "
+                            "(1 MiB); use b2_lm_head_argmax with a workspace",
+                            M, nb, kNoAllocKeys);
+    unsigned long long* part = nullptr;
+    int rc = noalloc_keys(&part);
+    if (rc) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (wtype) {
+        case B2_W_I8: rc = dispatch<B2_W_I8>(x, ldx, M, K, V, table, scales, norm_w, eps, logits, ldl, part, s); break;
+        case B2_W_F16: rc = dispatch<B2_W_F16>(x, ldx, M, K, V, table, scales, norm_w, eps, logits, ldl, part, s); break;
+        default: rc = dispatch<B2_W_F32>(x, ldx, M, K, V, table, scales, norm_w, eps, logits, ldl, part, s); break;
+    }
+    if (rc) return rc;
+    cudaError_t e = b2::launch_pdl(argmax_final_kernel, dim3(M), dim3(256), 0, s, (const unsigned long long*)part, nb,
+                                   tokens);
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_argmax_final: %s", cudaGetErrorString(e));
+    return 0;
+}

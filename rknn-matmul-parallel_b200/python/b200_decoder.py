@@ -126,6 +126,9 @@ SIGNATURES = {
     "b2_attention": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp]),
     "b2_lm_head_workspace": (c_size, [c_int, c_int]),
     "b2_loop_advance": (c_int, [c_vp, c_vp, c_int, c_vp]),
+    "b2_lm_head_noalloc_max_keys": (c_size, []),
+    "b2_lm_head_argmax_noalloc": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_float,
+                                          c_vp, c_int, c_vp, c_vp]),
     "b2_mk_check": (c_int, [c_vp]),
     "b2_mk_scratch_bytes": (c_size, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "b2_mk_decode": (c_int, [c_vp, c_vp]),
