@@ -161,17 +161,6 @@ __device__ __forceinline__ bool consumer_all(bool pred) {
 
 // ─── dot products from shared memory ───
 
-__device__ __forceinline__ float dot8h(const uint4 xv, const float (&w)[8], float acc) {
-    const uint32_t* xu = &xv.x;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        float2 x = b2::h2_to_f2(xu[i]);
-        acc = fmaf(x.x, w[2 * i], acc);
-        acc = fmaf(x.y, w[2 * i + 1], acc);
-    }
-    return acc;
-}
-
 template <int WT>
 __device__ __forceinline__ void expand8(const uint4 wv, int g, float (&w)[8]) {
     const uint32_t* u = &wv.x;
@@ -201,23 +190,56 @@ __host__ __device__ constexpr int elems16() {
     return WT == B2_W_F16 ? 8 : WT == B2_W_I8 ? 16 : 32;
 }
 
-// Warp-collective dot of one weight row in shared memory with the FP16
-// activation xs[K]; every lane returns the full sum.
-template <int WT>
-__device__ __forceinline__ float row_dot(const unsigned char* row, const __half* xs, int K, int lane) {
+// Warp-collective dots of NR weight rows (rows[i], i < nvalid) in shared
+// memory with the FP16 activation xs[K]; every lane gets the NR sums (rows at
+// i >= nvalid re-read row 0 and their sums are meaningless).  All NR
+// rows' 16-byte words of one step are loaded before any arithmetic, and each
+// activation word is converted once for all rows, so a warp keeps NR loads in
+// flight and spends its issue slots on FMAs.
+template <int WT, int NR>
+__device__ __forceinline__ void rows_dot(const unsigned char* const (&rows)[NR], int nvalid, const __half* xs,
+                                         int K, int lane, float (&out)[NR]) {
     constexpr int E = elems16<WT>();
     const int nch = K / E;
-    float acc = 0.f;
+    float acc[NR];
+    const unsigned char* rp[NR];
+#pragma unroll
+    for (int i = 0; i < NR; i++) {
+        acc[i] = 0.f;
+        rp[i] = i < nvalid ? rows[i] : rows[0];
+    }
+#pragma unroll 2
     for (int c = lane; c < nch; c += 32) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(row + (size_t)c * 16);
+        uint4 wv[NR];
+#pragma unroll
+        for (int i = 0; i < NR; i++)
+            wv[i] = *reinterpret_cast<const uint4*>(rp[i] + (size_t)c * 16);
 #pragma unroll
         for (int g = 0; g < E / 8; g++) {
-            float w[8];
-            expand8<WT>(wv, g, w);
-            acc = dot8h(*reinterpret_cast<const uint4*>(xs + c * E + g * 8), w, acc);
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + c * E + g * 8);
+            float xf[8];
+            const uint32_t* xu = &xv.x;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const float2 f = b2::h2_to_f2(xu[t]);
+                xf[2 * t] = f.x;
+                xf[2 * t + 1] = f.y;
+            }
+#pragma unroll
+            for (int i = 0; i < NR; i++) {
+                float w[8];
+                expand8<WT>(wv[i], g, w);
+#pragma unroll
+                for (int t = 0; t < 8; t++) acc[i] = fmaf(xf[t], w[t], acc[i]);
+            }
         }
     }
-    return b2::warp_sum(acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < NR; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+#pragma unroll
+    for (int i = 0; i < NR; i++) out[i] = acc[i];
 }
 
 __host__ __device__ inline size_t row_bytes(int wtype, int K) {
@@ -435,32 +457,37 @@ struct Consumer {
                     atomicOr(p.state + B2_MK_ERR, 1);
                     break;
                 }
-                __nanosleep(ns);
-                if (ns < 256) ns <<= 1;
+                if (it > 64) __nanosleep(ns);
+                if (ns < 128) ns <<= 1;
             }
-            __threadfence();
         }
         consumer_sync();
         aborted = *(volatile int*)&sh.cabort != 0;
     }
 
+    // After a CTA barrier, consumer 0's release publishes every consumer's
+    // prior stores (release is cumulative over what the barrier ordered).
     __device__ void signal(unsigned long long* cnt, unsigned long long amount) {
         consumer_sync();
-        if (tid == 0) {
-            __threadfence();
-            red_release(cnt, amount);
-        }
+        if (tid == 0) red_release(cnt, amount);
     }
 
-    // Stage src[0..K) (global, written by other CTAs) as FP16, optionally RMS-normalized.
+    // Stage src[0..K) (global, written by other CTAs) as FP16, optionally
+    // RMS-normalized.  K <= kMaxK and K % 8 == 0 (b2_mk_check), so each thread
+    // holds at most four float4 of src in registers: one L2 round trip.
     __device__ void stage_x(const float* src, int K, const float* norm_w) {
+        constexpr int kV = kMaxK / (4 * kConsumers);
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        float4 v[kV];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int q = tid + j * kConsumers;
+            v[j] = q * 4 < K ? __ldcg(s4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+        }
         float rms = 1.f;
         if (norm_w) {
-            float ss = 0.f;
-            for (int k = tid; k < K; k += kConsumers) {
-                const float x = __ldcg(src + k);
-                ss = fmaf(x, x, ss);
-            }
             ss = b2::warp_sum(ss);
             if (lane == 0) sh.red[warp] = ss;
             consumer_sync();
@@ -469,10 +496,21 @@ struct Consumer {
             for (int w = 0; w < kCWarps; w++) t += sh.red[w];
             rms = 1.0f / sqrtf(t / (float)K + p.eps);
         }
-        for (int k = tid; k < K; k += kConsumers) {
-            float x = __ldcg(src + k);
-            if (norm_w) x = (x * rms) * norm_w[k];
-            xs[k] = __float2half_rn(x);
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int q = tid + j * kConsumers;
+            if (q * 4 >= K) break;
+            float4 x = v[j];
+            if (norm_w) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + q);
+                x.x = (x.x * rms) * w.x;
+                x.y = (x.y * rms) * w.y;
+                x.z = (x.z * rms) * w.z;
+                x.w = (x.w * rms) * w.w;
+            }
+            __half2* d = reinterpret_cast<__half2*>(xs + q * 4);
+            d[0] = __floats2half2_rn(x.x, x.y);
+            d[1] = __floats2half2_rn(x.z, x.w);
         }
         consumer_sync();
     }
@@ -546,11 +584,9 @@ struct Consumer {
             case IT_DN: rows_resid(c, buf, p.ffn, p.layers[c.l].dn, p.layers[c.l].dn_s, S.hbuf); break;
             case IT_LM: rows_lm(c, buf); break;
         }
-        consumer_sync();  // every consumer is done reading the stage
-        if (tid == 0) {
-            mbar_arrive(&sh.empty[stage]);
-            *(volatile int*)&sh.consumed = n + 1;
-        }
+        __syncwarp();  // this warp is done reading the stage
+        if (lane == 0) mbar_arrive(&sh.empty[stage]);
+        if (tid == 0) *(volatile int*)&sh.consumed = n + 1;
         n++;
     }
 
@@ -561,7 +597,6 @@ struct Consumer {
                 // rows of kv group g: q heads [g*Gq, (g+1)*Gq), k head g, v head g
                 consumer_sync();
                 if (tid == 0) {
-                    __threadfence();
                     for (int g = 0; g < p.nkv; g++) {
                         const int q0 = g * geo.Gq * kHD, q1 = q0 + geo.Gq * kHD;
                         const int k0 = geo.qd + g * kHD, v0 = geo.qd + geo.kvd + g * kHD;
@@ -604,13 +639,22 @@ struct Consumer {
         const size_t rb = row_bytes(WT, p.hidden);
         const float* sc = p.layers[c.l].qkv_s;
         float* out = S.qkv + (size_t)c.l * geo.nqkv;
-        for (int r = c.a + warp; r < c.b; r += kCWarps) {
-            const float d = row_dot<WT>(buf + (size_t)(r - c.a) * rb, xs, p.hidden, lane);
-            if (lane == 0) out[r] = sc ? d * sc[r] : d;
+        const int n = c.b - c.a;
+        for (int r0 = warp * 4; r0 < n; r0 += 4 * kCWarps) {
+            const unsigned char* rows[4] = {buf + (size_t)r0 * rb, buf + (size_t)(r0 + 1) * rb,
+                                            buf + (size_t)(r0 + 2) * rb, buf + (size_t)(r0 + 3) * rb};
+            float d[4];
+            rows_dot<WT, 4>(rows, min(4, n - r0), xs, p.hidden, lane, d);
+            if (lane < 4 && r0 + lane < n) {
+                const int r = c.a + r0 + lane;
+                const float v = lane == 0 ? d[0] : lane == 1 ? d[1] : lane == 2 ? d[2] : d[3];
+                out[r] = sc ? v * sc[r] : v;
+            }
         }
     }
 
-    // out[r] = resid[r] + s[r] * dot(row r, xs)  (o_proj into hmid, down into hbuf[l+1])
+    // out[r] = resid[r] + s[r] * dot(row r, xs)  (o_proj into hmid, down into hbuf[l+1]);
+    // these chunks hold few long rows, so one row per warp.
     __device__ void rows_resid(const Chunk& c, const unsigned char* buf, int K, const void*, const float* sc,
                                float* dst_base) {
         const size_t rb = row_bytes(WT, K);
@@ -619,11 +663,10 @@ struct Consumer {
         float* dst = c.type == IT_O ? S.hmid + (size_t)c.l * H : S.hbuf + (size_t)(c.l + 1) * H;
         (void)dst_base;
         for (int r = c.a + warp; r < c.b; r += kCWarps) {
-            float d = row_dot<WT>(buf + (size_t)(r - c.a) * rb, xs, K, lane);
-            if (lane == 0) {
-                if (sc) d = d * sc[r];
-                dst[r] = __ldcg(resid + r) + d;
-            }
+            const unsigned char* rows[1] = {buf + (size_t)(r - c.a) * rb};
+            float d[1];
+            rows_dot<WT, 1>(rows, 1, xs, K, lane, d);
+            if (lane == 0) dst[r] = __ldcg(resid + r) + (sc ? d[0] * sc[r] : d[0]);
         }
     }
 
@@ -632,27 +675,43 @@ struct Consumer {
         const float* sc = p.layers[c.l].gu_s;
         float* act = S.act + (size_t)c.l * p.ffn;
         const int n = c.b - c.a;
-        for (int j = warp; j < n; j += kCWarps) {
-            float g = row_dot<WT>(buf + (size_t)j * rb, xs, p.hidden, lane);
-            float u = row_dot<WT>(buf + c.off1 + (size_t)j * rb, xs, p.hidden, lane);
-            if (lane == 0) {
+        for (int j0 = warp * 2; j0 < n; j0 += 2 * kCWarps) {
+            const int j1 = min(j0 + 1, n - 1);
+            const unsigned char* rows[4] = {buf + (size_t)j0 * rb, buf + c.off1 + (size_t)j0 * rb,
+                                            buf + (size_t)j1 * rb, buf + c.off1 + (size_t)j1 * rb};
+            float d[4];
+            rows_dot<WT, 4>(rows, j0 + 1 < n ? 4 : 2, xs, p.hidden, lane, d);
+            if (lane < 2 && j0 + lane < n) {
+                const int j = c.a + j0 + lane;
+                float g = lane == 0 ? d[0] : d[2], u = lane == 0 ? d[1] : d[3];
                 if (sc) {
-                    g = g * sc[c.a + j];
-                    u = u * sc[p.ffn + c.a + j];
+                    g = g * sc[j];
+                    u = u * sc[p.ffn + j];
                 }
                 const float sig = 1.0f / (1.0f + expf(-g));
-                act[c.a + j] = (g * sig) * u;
+                act[j] = (g * sig) * u;
             }
         }
     }
 
     __device__ void rows_lm(const Chunk& c, const unsigned char* buf) {
-        for (int r = c.a + warp; r < c.b; r += kCWarps) {
-            const float d = row_dot<B2_W_I8>(buf + (size_t)(r - c.a) * p.hidden, xs, p.hidden, lane);
-            const float logit = d * p.lm_s[r];
-            if (lane == 0 && p.logits) p.logits[r] = logit;
-            const unsigned long long k = b2::argmax_key(logit, (uint32_t)r);
-            best = k > best ? k : best;
+        const int n = c.b - c.a;
+        const size_t rb = (size_t)p.hidden;
+        for (int r0 = warp * 4; r0 < n; r0 += 4 * kCWarps) {
+            const unsigned char* rows[4] = {buf + (size_t)r0 * rb, buf + (size_t)(r0 + 1) * rb,
+                                            buf + (size_t)(r0 + 2) * rb, buf + (size_t)(r0 + 3) * rb};
+            float d[4];
+            const int nv = min(4, n - r0);
+            rows_dot<B2_W_I8, 4>(rows, nv, xs, p.hidden, lane, d);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (i >= nv) break;
+                const int r = c.a + r0 + i;
+                const float logit = d[i] * p.lm_s[r];
+                if (lane == i && p.logits) p.logits[r] = logit;
+                const unsigned long long k = b2::argmax_key(logit, (uint32_t)r);
+                best = k > best ? k : best;
+            }
         }
     }
 
@@ -897,7 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
     if (tid == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], 1);
+            mbar_init(&sh.empty[s], kCWarps);
         }
         sh.abort = 0;
         sh.cabort = 0;
