@@ -85,6 +85,79 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
     return __half22float2(h);
 }
 
+// ── Exact weight expansion with integer/logic instructions only ──
+// The GEMV inner loops are issue-bound on type conversions, so weights are
+// widened to FP32 by bit manipulation instead.  All three forms are exact.
+//
+// F16 (exponent rebias by multiplication, F. Giesen, "Half to float done
+// quic", 2012): moving a half's exponent+mantissa up 13 bits and keeping its
+// sign gives an FP32 whose value is the half's times 2^-112 (subnormal halves
+// become FP32 denormals, also exact).  The 2^112 is folded into the staged
+// activation instead (kF16XScale), so a dot product needs no multiply here.
+// Finite halves only (weights are finite).
+constexpr float kF16XScale = 0x1p112f;
+__device__ __forceinline__ float f16lo_scaled(uint32_t u) {
+    return __uint_as_float(((u << 13) & 0x0FFFE000u) | ((u << 16) & 0x80000000u));
+}
+__device__ __forceinline__ float f16hi_scaled(uint32_t u) {
+    return __uint_as_float(((u >> 3) & 0x0FFFE000u) | (u & 0x80000000u));
+}
+
+// INT8 / INT4 (the "magic number" method): an unsigned integer n < 2^23
+// placed in the mantissa of 2^23 (bits 0x4B000000 | n) reads as 2^23 + n,
+// and one FP32 subtraction removes the bias exactly.  Signed values are made
+// unsigned by flipping the top bit of each field (s + 128, s + 8).
+__device__ __forceinline__ uint32_t i8x4_bias(uint32_t w) { return w ^ 0x80808080u; }
+template <int I>
+__device__ __forceinline__ float i8_from_biased(uint32_t u) {
+    return __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u | I)) - 8388736.0f;  // 2^23 + 128
+}
+__device__ __forceinline__ uint32_t i4x8_bias(uint32_t w) { return w ^ 0x88888888u; }
+template <int I>
+__device__ __forceinline__ float i4_from_biased(uint32_t u) {
+    return __uint_as_float(((u >> (4 * I)) & 0xFu) | 0x4B000000u) - 8388616.0f;  // 2^23 + 8
+}
+
+// Eight consecutive weights of one 16-byte chunk (group g of 8) as FP32.
+// F16 values come out scaled by 2^-112 (pair them with kF16XScale).
+template <int WT>
+__device__ __forceinline__ void expand8_exact(const uint4 wv, int g, float (&w)[8]) {
+    const uint32_t* u = &wv.x;
+    if constexpr (WT == B2_W_F16) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = f16lo_scaled(u[i]);
+            w[2 * i + 1] = f16hi_scaled(u[i]);
+        }
+    } else if constexpr (WT == B2_W_I8) {
+        const uint32_t a = i8x4_bias(u[2 * g]), b = i8x4_bias(u[2 * g + 1]);
+        w[0] = i8_from_biased<0>(a);
+        w[1] = i8_from_biased<1>(a);
+        w[2] = i8_from_biased<2>(a);
+        w[3] = i8_from_biased<3>(a);
+        w[4] = i8_from_biased<0>(b);
+        w[5] = i8_from_biased<1>(b);
+        w[6] = i8_from_biased<2>(b);
+        w[7] = i8_from_biased<3>(b);
+    } else {  // int4: word g holds 8 nibbles, element i at bits [4i, 4i+4)
+        const uint32_t a = i4x8_bias(u[g]);
+        w[0] = i4_from_biased<0>(a);
+        w[1] = i4_from_biased<1>(a);
+        w[2] = i4_from_biased<2>(a);
+        w[3] = i4_from_biased<3>(a);
+        w[4] = i4_from_biased<4>(a);
+        w[5] = i4_from_biased<5>(a);
+        w[6] = i4_from_biased<6>(a);
+        w[7] = i4_from_biased<7>(a);
+    }
+}
+
+// Activation scale that pairs with expand8_exact<WT>.
+template <int WT>
+__host__ __device__ constexpr float x_scale() {
+    return WT == B2_W_F16 ? kF16XScale : 1.0f;
+}
+
 // Orderable encoding of a float: a larger float maps to a larger unsigned.
 __device__ __forceinline__ uint32_t float_order(float f) {
     uint32_t u = __float_as_uint(f);

@@ -43,24 +43,30 @@ constexpr int kThreads = kConsumers + 32;
 constexpr int kStages = 6;
 constexpr int kStageBytes = 32 * 1024;
 constexpr int kHD = 128;
-constexpr int kMaxK = 4096;        // longest activation staged as FP16
+constexpr int kMaxK = 3072;        // longest staged activation (hidden, q_dim, ffn)
+constexpr int kV = kMaxK / (4 * kConsumers);  // float4 groups of a staged vector per consumer thread
 constexpr int kMaxSplit = 32;      // attention position ranges per kv head
-constexpr int kCntPerLayer = 32;   // u64 counters per layer
 constexpr int kMaxGq = 2;          // q heads per kv head handled by one attention unit
-constexpr long long kPollLimit = 1ll << 23;
+constexpr int kScCap = 1040;       // per-item scales prefetched into shared memory
+constexpr int kResCap = 64;        // per-item residual rows prefetched into shared memory
+constexpr long long kPollLimit = 1ll << 22;
 constexpr long long kBarLimit = 1ll << 22;
 
-enum { C_QKV = 0, C_ATTN = 8, C_ATTN_DONE = 16, C_O = 17, C_GU = 18, C_DN = 19 };
 enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM };
 
+// Vectors passed between CTAs are "LL" words (the low-latency protocol of
+// NCCL's LL transport): one 64-bit store holds an FP32 value in the low half
+// and the step's generation tag in the high half.  A reader polls the words
+// it needs until every tag is this step's, so producers need no fence and no
+// flag, and a consumer starts as soon as its own inputs have landed.
 struct Scratch {
-    unsigned long long* cnt;  // [L][kCntPerLayer] + [8] globals
-    float* hbuf;              // [L+1][H]
-    float* hmid;              // [L][H]
-    float* qkv;               // [L][qd + 2 kvd]
-    float* attn;              // [L][qd]
-    float* act;               // [L][F]
-    float* part;              // [L][nkv][kMaxSplit][Gq][2 + hd]
+    unsigned long long* cnt;   // [8]: [0] CTAs finished, [1] best argmax key
+    unsigned long long* hbuf;  // LL [L+1][H] layer inputs (row 0 unused: layer 0 reads the embedding)
+    unsigned long long* hmid;  // LL [L][H] hidden after attention + residual
+    unsigned long long* qkv;   // LL [L][qd + 2 kvd]
+    unsigned long long* part;  // LL [L][nkv][kMaxSplit][Gq][2 + hd] attention partials (m, l, o[hd])
+    unsigned long long* act;   // LL [L][F] SiLU(gate) * up
+    float* hfinal;             // [H] final hidden state (plain FP32, read by the host)
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -71,20 +77,18 @@ __host__ __device__ inline Scratch scratch_layout(void* base, int L, int H, int 
     size_t off = 0;
     Scratch s;
     const size_t qd = (size_t)nq * hd, kvd = (size_t)nkv * hd;
-    s.cnt = reinterpret_cast<unsigned long long*>(p + off);
-    off += align256(((size_t)L * kCntPerLayer + 8) * 8);
-    s.hbuf = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)(L + 1) * H * 4);
-    s.hmid = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)L * H * 4);
-    s.qkv = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)L * (qd + 2 * kvd) * 4);
-    s.attn = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)L * qd * 4);
-    s.act = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)L * F * 4);
-    s.part = reinterpret_cast<float*>(p + off);
-    off += align256((size_t)L * nkv * kMaxSplit * (nq / nkv) * (2 + hd) * 4);
+    auto take = [&](size_t bytes) {
+        unsigned char* r = p + off;
+        off += align256(bytes);
+        return r;
+    };
+    s.cnt = reinterpret_cast<unsigned long long*>(take(8 * 8));
+    s.hbuf = reinterpret_cast<unsigned long long*>(take((size_t)(L + 1) * H * 8));
+    s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)L * H * 8));
+    s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)L * (qd + 2 * kvd) * 8));
+    s.part = reinterpret_cast<unsigned long long*>(take((size_t)L * nkv * kMaxSplit * (nq / nkv) * (2 + hd) * 8));
+    s.act = reinterpret_cast<unsigned long long*>(take((size_t)L * F * 8));
+    s.hfinal = reinterpret_cast<float*>(take((size_t)H * 4));
     if (total) *total = off;
     return s;
 }
@@ -128,16 +132,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void red_release(unsigned long long* p, unsigned long long v) {
-    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 __device__ __forceinline__ unsigned long long atom_add_acqrel(unsigned long long* p, unsigned long long v) {
     unsigned long long old;
     asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
@@ -159,87 +153,122 @@ __device__ __forceinline__ bool consumer_all(bool pred) {
     return r != 0;
 }
 
+// ── LL words ──
+__device__ __forceinline__ void ll_put(unsigned long long* p, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_get(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Two adjacent words (16-byte aligned); each word is read atomically.
+__device__ __forceinline__ ulonglong2 ll_get2(const unsigned long long* p) {
+    ulonglong2 r;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ bool ll_ok(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
 // ─── dot products from shared memory ───
 
+// ─── tensor-core row dots ───
+//
+// mma.m16n8k16 (FP16 operands, FP32 accumulation: every product is exact and
+// the sum is FP32, the reference's matmul numerics) takes 16 weight rows at
+// once: the rows are the A operand and the staged FP16 activation, repeated
+// in all 8 columns, the B operand.  Each row is cut into 64-byte
+// super-blocks; lane (g = lane / 4, q = lane % 4) feeds rows g and g + 8
+// with the 16 bytes at offset 16 q of every super-block and takes the
+// activation elements of the same k positions.  Inside a super-block the
+// k order is permuted identically for A and B, which a dot product does
+// not see.  Int8 and int4 weights widen to FP16 exactly with byte permutes
+// (the value plus 1024 sits in the mantissa of 1024, one half2 subtraction
+// removes the bias).
+
 template <int WT>
-__device__ __forceinline__ void expand8(const uint4 wv, int g, float (&w)[8]) {
-    const uint32_t* u = &wv.x;
+__host__ __device__ constexpr int sb_k() {  // k positions per 64-byte super-block
+    return WT == B2_W_F16 ? 32 : WT == B2_W_I8 ? 64 : 128;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// One super-block of rows g and g + 8 (wg, wh: this lane's 16 bytes of each)
+// against this lane's activation words xw; consecutive steps alternate
+// between two accumulators so neighbouring MMAs do not wait on each other.
+template <int WT>
+__device__ __forceinline__ void sb_mma(float (&d0)[4], float (&d1)[4], const uint4 wg, const uint4 wh,
+                                       const uint32_t* xw) {
+    const uint32_t* g = &wg.x;
+    const uint32_t* h = &wh.x;
     if constexpr (WT == B2_W_F16) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float2 f = b2::h2_to_f2(u[i]);
-            w[2 * i] = f.x;
-            w[2 * i + 1] = f.y;
-        }
+        mma16816(d0, g[0], h[0], g[1], h[1], xw[0], xw[1]);
+        mma16816(d1, g[2], h[2], g[3], h[3], xw[2], xw[3]);
     } else if constexpr (WT == B2_W_I8) {
-        const uint32_t a = u[2 * g], b = u[2 * g + 1];
+        const uint32_t bias = 0x64806480u;  // half2(1152, 1152) = 1024 + 128
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            w[i] = (float)(int8_t)(a >> (8 * i));
-            w[4 + i] = (float)(int8_t)(b >> (8 * i));
+        for (int t = 0; t < 4; t++) {
+            const uint32_t ug = g[t] ^ 0x80808080u, uh = h[t] ^ 0x80808080u;
+            const uint32_t glo = hsub2_u32(__byte_perm(ug, 0x64646464u, 0x4140), bias);
+            const uint32_t ghi = hsub2_u32(__byte_perm(ug, 0x64646464u, 0x4342), bias);
+            const uint32_t hlo = hsub2_u32(__byte_perm(uh, 0x64646464u, 0x4140), bias);
+            const uint32_t hhi = hsub2_u32(__byte_perm(uh, 0x64646464u, 0x4342), bias);
+            mma16816(t & 1 ? d1 : d0, glo, hlo, ghi, hhi, xw[2 * t], xw[2 * t + 1]);
         }
     } else {
-        const uint32_t a = u[g];
+        const uint32_t bias = 0x64086408u;  // half2(1032, 1032) = 1024 + 8
 #pragma unroll
-        for (int i = 0; i < 8; i++) w[i] = (float)(((int32_t)(a << (28 - 4 * i))) >> 28);
-    }
-}
-
-template <int WT>
-__host__ __device__ constexpr int elems16() {
-    return WT == B2_W_F16 ? 8 : WT == B2_W_I8 ? 16 : 32;
-}
-
-// Warp-collective dots of NR weight rows (rows[i], i < nvalid) in shared
-// memory with the FP16 activation xs[K]; every lane gets the NR sums (rows at
-// i >= nvalid re-read row 0 and their sums are meaningless).  All NR
-// rows' 16-byte words of one step are loaded before any arithmetic, and each
-// activation word is converted once for all rows, so a warp keeps NR loads in
-// flight and spends its issue slots on FMAs.
-template <int WT, int NR>
-__device__ __forceinline__ void rows_dot(const unsigned char* const (&rows)[NR], int nvalid, const __half* xs,
-                                         int K, int lane, float (&out)[NR]) {
-    constexpr int E = elems16<WT>();
-    const int nch = K / E;
-    float acc[NR];
-    const unsigned char* rp[NR];
-#pragma unroll
-    for (int i = 0; i < NR; i++) {
-        acc[i] = 0.f;
-        rp[i] = i < nvalid ? rows[i] : rows[0];
-    }
-#pragma unroll 2
-    for (int c = lane; c < nch; c += 32) {
-        uint4 wv[NR];
-#pragma unroll
-        for (int i = 0; i < NR; i++)
-            wv[i] = *reinterpret_cast<const uint4*>(rp[i] + (size_t)c * 16);
-#pragma unroll
-        for (int g = 0; g < E / 8; g++) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + c * E + g * 8);
-            float xf[8];
-            const uint32_t* xu = &xv.x;
-#pragma unroll
-            for (int t = 0; t < 4; t++) {
-                const float2 f = b2::h2_to_f2(xu[t]);
-                xf[2 * t] = f.x;
-                xf[2 * t + 1] = f.y;
-            }
-#pragma unroll
-            for (int i = 0; i < NR; i++) {
-                float w[8];
-                expand8<WT>(wv[i], g, w);
-#pragma unroll
-                for (int t = 0; t < 8; t++) acc[i] = fmaf(xf[t], w[t], acc[i]);
-            }
+        for (int t = 0; t < 4; t++) {
+            const uint32_t ug = g[t] ^ 0x88888888u, uh = h[t] ^ 0x88888888u;
+            // word t holds k = 8t + i at nibble i; half2 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7)
+            mma16816(d0, hsub2_u32((ug & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32((uh & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32(((ug >> 4) & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32(((uh >> 4) & 0x000F000Fu) | 0x64006400u, bias), xw[4 * t], xw[4 * t + 1]);
+            mma16816(d1, hsub2_u32(((ug >> 8) & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32(((uh >> 8) & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32(((ug >> 12) & 0x000F000Fu) | 0x64006400u, bias),
+                     hsub2_u32(((uh >> 12) & 0x000F000Fu) | 0x64006400u, bias), xw[4 * t + 2], xw[4 * t + 3]);
         }
     }
+}
+
+// Dots of rows rg (row g) and rh (row g + 8) over super-blocks [s0, s1)
+// with the staged activation xs (FP16, in the k order sb_mma expects).
+// Returns this lane's row-g sum in out[0] and row-(g+8) sum in out[1].
+template <int WT>
+__device__ __forceinline__ void tile_dot(const unsigned char* rg, const unsigned char* rh, const __half* xs,
+                                         int s0, int s1, int lane, float (&out)[2]) {
+    constexpr int XW = sb_k<WT>() / 8;  // activation words (half2) per lane per super-block
+    const int q = lane & 3;
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int sb = s0; sb < s1; sb++) {
+        const uint4 wg = *reinterpret_cast<const uint4*>(rg + sb * 64 + q * 16);
+        const uint4 wh = *reinterpret_cast<const uint4*>(rh + sb * 64 + q * 16);
+        uint32_t xw[XW];
+        const uint4* xp = reinterpret_cast<const uint4*>(xs + sb * sb_k<WT>() + q * (sb_k<WT>() / 4));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < NR; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-#pragma unroll
-    for (int i = 0; i < NR; i++) out[i] = acc[i];
+        for (int i = 0; i < XW / 4; i++) *reinterpret_cast<uint4*>(xw + 4 * i) = xp[i];
+        sb_mma<WT>(d0, d1, wg, wh, xw);
+    }
+    // all 8 columns hold the same sums: column 2q of rows g and g + 8
+    out[0] = d0[0] + d1[0];
+    out[1] = d0[2] + d1[2];
 }
 
 __host__ __device__ inline size_t row_bytes(int wtype, int K) {
@@ -274,8 +303,9 @@ template <int WT, class V>
 __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
     const int H = p.hidden, F = p.ffn;
     const size_t rb_h = row_bytes(WT, H), rb_q = row_bytes(WT, geo.qd), rb_f = row_bytes(WT, F);
-    const int cap_h = kStageBytes / (int)rb_h, cap_q = kStageBytes / (int)rb_q, cap_f = kStageBytes / (int)rb_f;
-    const int cap_pair = kStageBytes / (2 * (int)rb_h);
+    // rows per stage, at most 64 (four 16-row tensor-core tiles)
+    const int cap_h = min(64, kStageBytes / (int)rb_h), cap_q = min(64, kStageBytes / (int)rb_q);
+    const int cap_f = min(64, kStageBytes / (int)rb_f), cap_pair = min(32, kStageBytes / (2 * (int)rb_h));
     for (int l = 0; l < p.n_layers; l++) {
         const B2MkLayer& Lw = p.layers[l];
         if (v.stop()) return;
@@ -349,7 +379,7 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
         Item it{IT_LM, p.n_layers, split_lo(p.vocab, geo.G, geo.cta), split_lo(p.vocab, geo.G, geo.cta + 1), 0, 0,
                 0, 0};
         v.begin(it);
-        const int cap = kStageBytes / H;  // int8 rows
+        const int cap = min(64, kStageBytes / H);  // int8 rows
         for (int a = it.r0; a < it.r1 && !v.stop(); a += cap) {
             const int b = min(it.r1, a + cap);
             Chunk c{IT_LM, p.n_layers, a, b, 0, 0, (const unsigned char*)p.lm + (size_t)a * H,
@@ -364,15 +394,17 @@ struct Shared {
     uint64_t full[kStages];
     uint64_t empty[kStages];
     int abort;                  // set by the producer (or a consumer) to stop the CTA
-    int cabort;                 // consumers' decision, written by consumer 0 before a barrier
+    int cabort;                 // consumers gave up (read by the producer)
     int issued, consumed;
-    int last;                   // this CTA was the last arriver of a group
     float red[kCWarps];
     unsigned long long best[kCWarps];
     float q[kMaxGq][kHD];                  // normalized + rotated q heads of the group
     float k[kHD], v[kHD];                  // new k (rotated) and v of the kv head
     float gm[kCWarps][kMaxGq], gl[kCWarps][kMaxGq];  // per-warp softmax state
     float go[kCWarps][kMaxGq][kHD];                   // per-warp partial outputs
+    float pr[kCWarps][16];      // per-warp partial row sums of a chunk
+    float sc[2][kScCap];        // prefetched scales of the current / next item
+    float res[2][kResCap];      // prefetched residual rows of the current / next item
 };
 
 __device__ __forceinline__ void set_error(const B2MkPlan& p, Shared& sh, int code) {
@@ -430,10 +462,13 @@ struct Consumer {
     unsigned char* ring;
     __half* xs;
     const Scratch& S;
-    unsigned long long target;  // per-CTA counter target multiplier: gen + 1
+    uint32_t tag;  // generation tag of this step's LL words
     const float* emb_row;
     int tid, lane, warp;
-    int n = 0;
+    int n = 0;       // chunks consumed
+    int items = 0;   // items begun; its parity selects the prefetch buffers
+    int buf = 0, r0 = 0, nrows = 0;  // current item: prefetch buffer, first row, row count
+    const float* isc = nullptr;       // current item's scale array (null: FP16 weights)
     // attention state of this thread's lane group (positions of group grp)
     float m_[kMaxGq], l_[kMaxGq], o_[kMaxGq][16], qv_[kMaxGq][16];
     unsigned long long best = 0ull;
@@ -441,53 +476,200 @@ struct Consumer {
 
     __device__ bool stop() const { return aborted; }
 
-    // Consumer 0 waits until *cnt >= want (or gives up); the decision reaches
-    // every consumer through shared memory across a barrier.
-    __device__ void wait_counter(const unsigned long long* cnt, unsigned long long want) {
+    __device__ bool abort_seen() const {
+        return *(volatile int*)&sh.abort || *(volatile const int*)(p.state + B2_MK_ERR);
+    }
+
+    // Every consumer votes; a failed wait anywhere stops the whole CTA.
+    __device__ void settle(bool ok) {
+        if (consumer_all(ok)) return;
         if (tid == 0) {
-            long long it = 0;
-            unsigned ns = 32;
-            while (ld_acquire(cnt) < want) {
-                if (*(volatile int*)&sh.abort || *(volatile int*)(p.state + B2_MK_ERR)) {
-                    sh.cabort = 1;
+            sh.cabort = 1;
+            atomicOr(p.state + B2_MK_ERR, 1);
+        }
+        aborted = true;
+    }
+
+    // Bounded poll of one LL word.
+    __device__ bool ll_wait(const unsigned long long* w, float& out) const {
+        for (long long it = 0;; it++) {
+            const unsigned long long v = ll_get(w);
+            if (ll_ok(v, tag)) {
+                out = ll_val(v);
+                return true;
+            }
+            if (it > kPollLimit || ((it & 63) == 63 && abort_seen())) return false;
+            __nanosleep(64);
+        }
+    }
+
+    // Lane 0 polls one word until it carries the tag; the lanes wait for it
+    // with the warp.  Only one request per warp and round reaches the L2
+    // (148 CTAs x 256 threads polling the same lines would congest it).
+    __device__ bool warp_lead_wait(const unsigned long long* w, bool has_word) const {
+        bool ok = true;
+        if (lane == 0 && has_word) {
+            for (long long it = 0;; it++) {
+                if (ll_ok(ll_get(w), tag)) break;
+                if (it > kPollLimit || ((it & 63) == 63 && abort_seen())) {
+                    ok = false;
                     break;
                 }
-                if (++it > kPollLimit) {
-                    sh.cabort = 1;
-                    atomicOr(p.state + B2_MK_ERR, 1);
-                    break;
-                }
-                if (it > 64) __nanosleep(ns);
-                if (ns < 128) ns <<= 1;
+                __nanosleep(96);
             }
         }
-        consumer_sync();
-        aborted = *(volatile int*)&sh.cabort != 0;
+        return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
 
-    // After a CTA barrier, consumer 0's release publishes every consumer's
-    // prior stores (release is cumulative over what the barrier ordered).
-    __device__ void signal(unsigned long long* cnt, unsigned long long amount) {
-        consumer_sync();
-        if (tid == 0) red_release(cnt, amount);
+    // This thread's float4 groups q = tid + j * kConsumers (elements 4q..4q+3)
+    // of the LL vector src[0..K), polled until every word carries the tag.
+    // The warp's first word gates the first read; writers of neighbouring
+    // rows finish together, so the rest is almost always already there.
+    __device__ bool ll_gather(const unsigned long long* src, int K, float4 (&v)[kV]) const {
+        if (!warp_lead_wait(src + (size_t)(warp * 32) * 4, warp * 32 * 4 < K)) return false;
+        unsigned pending = 0;
+#pragma unroll
+        for (int j = 0; j < kV; j++)
+            if ((tid + j * kConsumers) * 4 < K) pending |= 1u << j;
+        for (long long it = 0; pending; it++) {
+#pragma unroll
+            for (int j = 0; j < kV; j++) {
+                if (!((pending >> j) & 1)) continue;
+                const unsigned long long* w = src + (size_t)(tid + j * kConsumers) * 4;
+                const ulonglong2 a = ll_get2(w), b = ll_get2(w + 2);
+                if (ll_ok(a.x, tag) && ll_ok(a.y, tag) && ll_ok(b.x, tag) && ll_ok(b.y, tag)) {
+                    v[j] = make_float4(ll_val(a.x), ll_val(a.y), ll_val(b.x), ll_val(b.y));
+                    pending &= ~(1u << j);
+                }
+            }
+            if (!pending) break;
+            if (it > kPollLimit || ((it & 63) == 63 && abort_seen())) return false;
+            __nanosleep(128);
+        }
+        return true;
     }
 
-    // Stage src[0..K) (global, written by other CTAs) as FP16, optionally
-    // RMS-normalized.  K <= kMaxK and K % 8 == 0 (b2_mk_check), so each thread
-    // holds at most four float4 of src in registers: one L2 round trip.
-    __device__ void stage_x(const float* src, int K, const float* norm_w) {
-        constexpr int kV = kMaxK / (4 * kConsumers);
-        const float4* s4 = reinterpret_cast<const float4*>(src);
-        float4 v[kV];
-        float ss = 0.f;
+    // Same groups of a plain FP32 vector that is constant during the launch.
+    __device__ void plain_gather(const float* src, int K, float4 (&v)[kV]) const {
 #pragma unroll
         for (int j = 0; j < kV; j++) {
             const int q = tid + j * kConsumers;
-            v[j] = q * 4 < K ? __ldcg(s4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-            ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+            if (q * 4 < K) v[j] = __ldg(reinterpret_cast<const float4*>(src) + q);
         }
+    }
+
+    // The attention output of layer l (q_dim values) for this thread's groups:
+    // the S position-range partials of each head merged with the online
+    // softmax rule (the split-KV combine of flash decoding).  The poll only
+    // checks tags; the merge re-reads the (now cached) words.
+    __device__ const unsigned long long* part_rec(int l, int e, int s) const {
+        const int Gq = geo.Gq, hq = e / kHD, g = hq / Gq, h = hq % Gq;
+        return S.part + ((((size_t)l * p.nkv + g) * kMaxSplit + s) * Gq + h) * (2 + kHD);
+    }
+    __device__ bool attn_gather(int l, float4 (&v)[kV]) const {
+        if (!warp_lead_wait(part_rec(l, warp * 32 * 4, geo.S - 1), warp * 32 * 4 < geo.qd)) return false;
+        for (int j = 0; j < kV; j++) {
+            const int e = (tid + j * kConsumers) * 4;
+            if (e >= geo.qd) break;
+            const int d = e % kHD;
+            for (int s = 0; s < geo.S; s++) {
+                const unsigned long long* rec = part_rec(l, e, s);
+                for (long long it = 0;; it++) {
+                    const ulonglong2 ml = ll_get2(rec), o01 = ll_get2(rec + 2 + d), o23 = ll_get2(rec + 4 + d);
+                    if (ll_ok(ml.x, tag) && ll_ok(ml.y, tag) && ll_ok(o01.x, tag) && ll_ok(o01.y, tag) &&
+                        ll_ok(o23.x, tag) && ll_ok(o23.y, tag))
+                        break;
+                    if (it > kPollLimit || ((it & 63) == 63 && abort_seen())) return false;
+                    __nanosleep(128);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int e = (tid + j * kConsumers) * 4;
+            if (e >= geo.qd) break;
+            const int d = e % kHD;
+            float M = -INFINITY, den = 0.f;
+            float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < geo.S; s++) {
+                const unsigned long long* rec = part_rec(l, e, s);
+                const ulonglong2 ml = ll_get2(rec);
+                const float m = ll_val(ml.x);
+                if (m == -INFINITY) continue;
+                const ulonglong2 o01 = ll_get2(rec + 2 + d), o23 = ll_get2(rec + 4 + d);
+                const float Mn = fmaxf(M, m);
+                const float a = M == -INFINITY ? 0.f : expf(M - Mn);
+                const float b = expf(m - Mn);
+                den = den * a + ll_val(ml.y) * b;
+                num.x = num.x * a + ll_val(o01.x) * b;
+                num.y = num.y * a + ll_val(o01.y) * b;
+                num.z = num.z * a + ll_val(o23.x) * b;
+                num.w = num.w * a + ll_val(o23.y) * b;
+                M = Mn;
+            }
+            v[j] = make_float4(num.x / den, num.y / den, num.z / den, num.w / den);
+        }
+        return true;
+    }
+
+    // Static per-item inputs, requested before the item's wait so their
+    // latency hides behind it.  Norm weights are only pulled into L1 (this
+    // thread's 16-byte groups; registers are the scarce resource here) and
+    // read again by stage().
+    __device__ void load_norm(const float* nw, int K) {
+        if (!nw) return;
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int q = tid + j * kConsumers;
+            if (q * 4 < K) asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const float4*>(nw) + q));
+        }
+    }
+    // scales of rows [r0, r0 + nrows) (then of rows [r0 + off2, ...) when off2 > 0)
+    __device__ void load_scales(const float* sc, int off2) {
+        const int tot = off2 > 0 ? 2 * nrows : nrows;
+        if (!sc || tot > kScCap) return;
+        for (int i = tid; i < tot; i += kConsumers)
+            sh.sc[buf][i] = __ldg(sc + (i < nrows ? r0 + i : r0 + off2 + (i - nrows)));
+    }
+    __device__ float scale(const float* sc, int i, int off2) const {  // i-th scale of the item
+        if (!sc) return 1.f;
+        const int tot = off2 > 0 ? 2 * nrows : nrows;
+        if (tot <= kScCap) return sh.sc[buf][i];
+        return __ldg(sc + (i < nrows ? r0 + i : r0 + off2 + (i - nrows)));
+    }
+    // residual rows of the item: LL words already validated by this CTA's
+    // previous stage (so the poll ends at once), or the plain embedding row
+    __device__ bool load_res(const unsigned long long* ll, const float* plain) {
+        if (nrows > kResCap) return true;
+        bool ok = true;
+        for (int i = tid; i < nrows; i += kConsumers) {
+            float v = 0.f;
+            if (ll) ok = ll_wait(ll + r0 + i, v) && ok;
+            else v = __ldg(plain + r0 + i);
+            sh.res[buf][i] = v;
+        }
+        return ok;
+    }
+    __device__ float resid(const unsigned long long* ll, const float* plain, int i) const {
+        if (nrows <= kResCap) return sh.res[buf][i];
+        float v = 0.f;
+        if (!ll) return __ldg(plain + r0 + i);
+        ll_wait(ll + r0 + i, v);  // validated by this CTA's previous stage
+        return v;
+    }
+
+    // Optional RMSNorm (weights nw) and FP16 rounding into xs, in the k order
+    // the tensor-core dot of the coming rows expects: natural, or for int4
+    // rows each group of 8 as (0 4 1 5 2 6 3 7).  Runs after the vote, so
+    // every consumer has finished with the old xs.
+    __device__ void stage(const float4 (&v)[kV], int K, const float* nw, bool perm8) {
         float rms = 1.f;
-        if (norm_w) {
+        if (nw) {
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < kV; j++)
+                if ((tid + j * kConsumers) * 4 < K)
+                    ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
             ss = b2::warp_sum(ss);
             if (lane == 0) sh.red[warp] = ss;
             consumer_sync();
@@ -501,52 +683,80 @@ struct Consumer {
             const int q = tid + j * kConsumers;
             if (q * 4 >= K) break;
             float4 x = v[j];
-            if (norm_w) {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + q);
+            if (nw) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(nw) + q);
                 x.x = (x.x * rms) * w.x;
                 x.y = (x.y * rms) * w.y;
                 x.z = (x.z * rms) * w.z;
                 x.w = (x.w * rms) * w.w;
             }
-            __half2* d = reinterpret_cast<__half2*>(xs + q * 4);
-            d[0] = __floats2half2_rn(x.x, x.y);
-            d[1] = __floats2half2_rn(x.z, x.w);
+            if (perm8) {  // elements 4q..4q+3 are i = 0..3 or 4..7 of their group of 8
+                const int base = (q >> 1) * 8 + (q & 1);
+                xs[base] = __float2half_rn(x.x);
+                xs[base + 2] = __float2half_rn(x.y);
+                xs[base + 4] = __float2half_rn(x.z);
+                xs[base + 6] = __float2half_rn(x.w);
+            } else {
+                __half2* d = reinterpret_cast<__half2*>(xs + q * 4);
+                d[0] = __floats2half2_rn(x.x, x.y);
+                d[1] = __floats2half2_rn(x.z, x.w);
+            }
         }
         consumer_sync();
     }
 
-    __device__ const float* hidden_in(int l) const { return l == 0 ? emb_row : S.hbuf + (size_t)l * p.hidden; }
-
-    __device__ unsigned long long* cnt(int l, int c) const { return S.cnt + (size_t)l * kCntPerLayer + c; }
-
     __device__ void begin(const Item& it) {
+        buf = items & 1;
+        items++;
+        r0 = it.r0;
+        nrows = it.r1 - it.r0;
         const int H = p.hidden;
+        const B2MkLayer& Lw = p.layers[it.type == IT_LM ? 0 : it.l];
+        constexpr bool perm = WT == B2_W_I4;
+        float4 v[kV];
+        bool ok = true;
         switch (it.type) {
             case IT_QKV:
-                if (it.l > 0) wait_counter(cnt(it.l - 1, C_DN), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(hidden_in(it.l), H, p.layers[it.l].in_norm);
+                isc = Lw.qkv_s;
+                load_scales(Lw.qkv_s, 0);
+                load_norm(Lw.in_norm, H);
+                if (it.l == 0) plain_gather(emb_row, H, v);
+                else ok = ll_gather(S.hbuf + (size_t)it.l * H, H, v);
+                settle(ok);
+                if (!stop()) stage(v, H, Lw.in_norm, perm);
                 break;
-            case IT_ATTN: {
-                wait_counter(cnt(it.l, C_QKV + it.g), (unsigned long long)(geo.Gq + 2) * kHD * target);
-                if (stop()) return;
-                attn_prologue(it);
-                break;
-            }
+            case IT_ATTN: attn_prologue(it); break;
             case IT_O:
-                wait_counter(cnt(it.l, C_ATTN_DONE), (unsigned long long)p.nkv * target);
-                if (!stop()) stage_x(S.attn + (size_t)it.l * geo.qd, geo.qd, nullptr);
+                isc = Lw.o_s;
+                load_scales(Lw.o_s, 0);
+                ok = load_res(it.l == 0 ? nullptr : S.hbuf + (size_t)it.l * H, emb_row);
+                ok = attn_gather(it.l, v) && ok;
+                settle(ok);
+                if (!stop()) stage(v, geo.qd, nullptr, perm);
                 break;
             case IT_GU:
-                wait_counter(cnt(it.l, C_O), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(S.hmid + (size_t)it.l * H, H, p.layers[it.l].post_norm);
+                isc = Lw.gu_s;
+                load_scales(Lw.gu_s, p.ffn);
+                load_norm(Lw.post_norm, H);
+                ok = ll_gather(S.hmid + (size_t)it.l * H, H, v);
+                settle(ok);
+                if (!stop()) stage(v, H, Lw.post_norm, perm);
                 break;
             case IT_DN:
-                wait_counter(cnt(it.l, C_GU), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(S.act + (size_t)it.l * p.ffn, p.ffn, nullptr);
+                isc = Lw.dn_s;
+                load_scales(Lw.dn_s, 0);
+                ok = load_res(S.hmid + (size_t)it.l * H, nullptr);
+                ok = ll_gather(S.act + (size_t)it.l * p.ffn, p.ffn, v) && ok;
+                settle(ok);
+                if (!stop()) stage(v, p.ffn, nullptr, perm);
                 break;
             case IT_LM:
-                wait_counter(cnt(p.n_layers - 1, C_DN), (unsigned long long)geo.G * target);
-                if (!stop()) stage_x(S.hbuf + (size_t)p.n_layers * H, H, p.final_norm);
+                isc = p.lm_s;
+                load_scales(p.lm_s, 0);
+                load_norm(p.final_norm, H);
+                ok = ll_gather(S.hbuf + (size_t)p.n_layers * H, H, v);
+                settle(ok);
+                if (!stop()) stage(v, H, p.final_norm, false);  // int8 table
                 best = 0ull;
                 break;
         }
@@ -575,14 +785,14 @@ struct Consumer {
     __device__ void chunk(const Chunk& c) {
         const int stage = n % kStages;
         if (aborted || !wait_full(stage, (uint32_t)((n / kStages) & 1))) return;
-        const unsigned char* buf = ring + (size_t)stage * kStageBytes;
+        const unsigned char* buf_ = ring + (size_t)stage * kStageBytes;
         switch (c.type) {
-            case IT_QKV: rows_qkv(c, buf); break;
-            case IT_ATTN: attn_chunk(c, buf); break;
-            case IT_O: rows_resid(c, buf, geo.qd, p.layers[c.l].o, p.layers[c.l].o_s, S.hmid); break;
-            case IT_GU: rows_gu(c, buf); break;
-            case IT_DN: rows_resid(c, buf, p.ffn, p.layers[c.l].dn, p.layers[c.l].dn_s, S.hbuf); break;
-            case IT_LM: rows_lm(c, buf); break;
+            case IT_QKV: rows_qkv(c, buf_); break;
+            case IT_ATTN: attn_chunk(c, buf_); break;
+            case IT_O: rows_resid(c, buf_, geo.qd); break;
+            case IT_GU: rows_gu(c, buf_); break;
+            case IT_DN: rows_resid(c, buf_, p.ffn); break;
+            case IT_LM: rows_lm(c, buf_); break;
         }
         __syncwarp();  // this warp is done reading the stage
         if (lane == 0) mbar_arrive(&sh.empty[stage]);
@@ -590,175 +800,196 @@ struct Consumer {
         n++;
     }
 
+    // Rows publish their LL words as they are computed; only attention (its
+    // partial) and the lm_head (its argmax) have work at the end of an item.
     __device__ void end(const Item& it) {
         if (stop()) return;
-        switch (it.type) {
-            case IT_QKV: {
-                // rows of kv group g: q heads [g*Gq, (g+1)*Gq), k head g, v head g
-                consumer_sync();
-                if (tid == 0) {
-                    for (int g = 0; g < p.nkv; g++) {
-                        const int q0 = g * geo.Gq * kHD, q1 = q0 + geo.Gq * kHD;
-                        const int k0 = geo.qd + g * kHD, v0 = geo.qd + geo.kvd + g * kHD;
-                        int n_rows = max(0, min(it.r1, q1) - max(it.r0, q0)) +
-                                     max(0, min(it.r1, k0 + kHD) - max(it.r0, k0)) +
-                                     max(0, min(it.r1, v0 + kHD) - max(it.r0, v0));
-                        if (n_rows) red_release(cnt(it.l, C_QKV + g), (unsigned long long)n_rows);
-                    }
-                }
-                break;
-            }
-            case IT_ATTN: attn_epilogue(it); break;
-            case IT_O: signal(cnt(it.l, C_O), 1); break;
-            case IT_GU: signal(cnt(it.l, C_GU), 1); break;
-            case IT_DN: signal(cnt(it.l, C_DN), 1); break;
-            case IT_LM: {
-                unsigned long long b = best;
+        if (it.type == IT_ATTN) {
+            attn_epilogue(it);
+        } else if (it.type == IT_LM) {
+            unsigned long long b = best;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const unsigned long long x = __shfl_xor_sync(0xffffffffu, b, o);
-                    b = x > b ? x : b;
-                }
-                if (lane == 0) sh.best[warp] = b;
-                consumer_sync();
-                if (tid == 0) {
-                    unsigned long long m = 0ull;
-                    for (int w = 0; w < kCWarps; w++) m = sh.best[w] > m ? sh.best[w] : m;
-                    atomicMax(S.cnt + (size_t)p.n_layers * kCntPerLayer + 1, m);
-                }
-                break;
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long x = __shfl_xor_sync(0xffffffffu, b, o);
+                b = x > b ? x : b;
+            }
+            if (lane == 0) sh.best[warp] = b;
+            consumer_sync();
+            if (tid == 0) {
+                unsigned long long m = 0ull;
+                for (int w = 0; w < kCWarps; w++) m = sh.best[w] > m ? sh.best[w] : m;
+                atomicMax(S.cnt + 1, m);
             }
         }
     }
 
     // ── row kernels ──
 
-    __device__ float scale_of(const float* s, int r) const { return s ? s[r] : 1.f; }
-
-    __device__ void rows_qkv(const Chunk& c, const unsigned char* buf) {
-        const size_t rb = row_bytes(WT, p.hidden);
-        const float* sc = p.layers[c.l].qkv_s;
-        float* out = S.qkv + (size_t)c.l * geo.nqkv;
-        const int n = c.b - c.a;
-        for (int r0 = warp * 4; r0 < n; r0 += 4 * kCWarps) {
-            const unsigned char* rows[4] = {buf + (size_t)r0 * rb, buf + (size_t)(r0 + 1) * rb,
-                                            buf + (size_t)(r0 + 2) * rb, buf + (size_t)(r0 + 3) * rb};
-            float d[4];
-            rows_dot<WT, 4>(rows, min(4, n - r0), xs, p.hidden, lane, d);
-            if (lane < 4 && r0 + lane < n) {
-                const int r = c.a + r0 + lane;
-                const float v = lane == 0 ? d[0] : lane == 1 ? d[1] : lane == 2 ? d[2] : d[3];
-                out[r] = sc ? v * sc[r] : v;
+    // Sums of the chunk's nr rows (row(r) points at row r in the stage),
+    // split over the 8 warps by 16-row tile and super-block range; the
+    // partials meet in shared memory and thread r (< nr) receives row r.
+    template <int W, class RowPtr>
+    __device__ float chunk_dot(int nr, int K, RowPtr row) {
+        const int nt = (nr + 15) >> 4;  // <= 4 (a stage holds at most 64 rows)
+        const int ks = kCWarps / (nt == 3 ? 4 : nt);
+        const int tile = warp / ks, part = warp % ks;
+        if (tile < nt) {
+            const int nsb = K / sb_k<W>();
+            const int g = lane >> 2;
+            const int ra = min(tile * 16 + g, nr - 1), rb = min(tile * 16 + g + 8, nr - 1);
+            float o[2];
+            tile_dot<W>(row(ra), row(rb), xs, split_lo(nsb, ks, part), split_lo(nsb, ks, part + 1), lane, o);
+            if ((lane & 3) == 0) {
+                sh.pr[warp][g] = o[0];
+                sh.pr[warp][g + 8] = o[1];
             }
+        }
+        consumer_sync();
+        float sum = 0.f;
+        if (tid < nr) {
+            const int t = tid >> 4, r = tid & 15;
+            for (int w = t * ks; w < t * ks + ks; w++) sum += sh.pr[w][r];
+        }
+        return sum;
+    }
+
+    __device__ void rows_qkv(const Chunk& c, const unsigned char* buf_) {
+        const size_t rb = row_bytes(WT, p.hidden);
+        const int n = c.b - c.a;
+        const float v = chunk_dot<WT>(n, p.hidden, [&](int r) { return buf_ + (size_t)r * rb; });
+        if (tid < n) {
+            const int r = c.a + tid;
+            ll_put(S.qkv + (size_t)c.l * geo.nqkv + r, v * scale(isc, r - r0, 0), tag);
         }
     }
 
-    // out[r] = resid[r] + s[r] * dot(row r, xs)  (o_proj into hmid, down into hbuf[l+1]);
-    // these chunks hold few long rows, so one row per warp.
-    __device__ void rows_resid(const Chunk& c, const unsigned char* buf, int K, const void*, const float* sc,
-                               float* dst_base) {
+    // out[r] = resid[r] + s[r] * dot(row r, xs): o_proj into hmid, down into hbuf[l+1]
+    __device__ void rows_resid(const Chunk& c, const unsigned char* buf_, int K) {
         const size_t rb = row_bytes(WT, K);
-        const int H = p.hidden;
-        const float* resid = c.type == IT_O ? hidden_in(c.l) : S.hmid + (size_t)c.l * H;
-        float* dst = c.type == IT_O ? S.hmid + (size_t)c.l * H : S.hbuf + (size_t)(c.l + 1) * H;
-        (void)dst_base;
-        for (int r = c.a + warp; r < c.b; r += kCWarps) {
-            const unsigned char* rows[1] = {buf + (size_t)(r - c.a) * rb};
-            float d[1];
-            rows_dot<WT, 1>(rows, 1, xs, K, lane, d);
-            if (lane == 0) dst[r] = __ldcg(resid + r) + (sc ? d[0] * sc[r] : d[0]);
+        const int H = p.hidden, n = c.b - c.a;
+        const bool is_o = c.type == IT_O;
+        const float v = chunk_dot<WT>(n, K, [&](int r) { return buf_ + (size_t)r * rb; });
+        if (tid < n) {
+            const int r = c.a + tid;
+            const unsigned long long* res_ll =
+                is_o ? (c.l == 0 ? nullptr : S.hbuf + (size_t)c.l * H) : S.hmid + (size_t)c.l * H;
+            unsigned long long* dst = is_o ? S.hmid + (size_t)c.l * H : S.hbuf + (size_t)(c.l + 1) * H;
+            const float y = resid(res_ll, emb_row, r - r0) + v * scale(isc, r - r0, 0);
+            ll_put(dst + r, y, tag);
+            if (!is_o && c.l == p.n_layers - 1) S.hfinal[r] = y;
         }
     }
 
-    __device__ void rows_gu(const Chunk& c, const unsigned char* buf) {
+    // rows 2j / 2j+1 of the dot are gate / up of channel c.a + j
+    __device__ void rows_gu(const Chunk& c, const unsigned char* buf_) {
         const size_t rb = row_bytes(WT, p.hidden);
-        const float* sc = p.layers[c.l].gu_s;
-        float* act = S.act + (size_t)c.l * p.ffn;
         const int n = c.b - c.a;
-        for (int j0 = warp * 2; j0 < n; j0 += 2 * kCWarps) {
-            const int j1 = min(j0 + 1, n - 1);
-            const unsigned char* rows[4] = {buf + (size_t)j0 * rb, buf + c.off1 + (size_t)j0 * rb,
-                                            buf + (size_t)j1 * rb, buf + c.off1 + (size_t)j1 * rb};
-            float d[4];
-            rows_dot<WT, 4>(rows, j0 + 1 < n ? 4 : 2, xs, p.hidden, lane, d);
-            if (lane < 2 && j0 + lane < n) {
-                const int j = c.a + j0 + lane;
-                float g = lane == 0 ? d[0] : d[2], u = lane == 0 ? d[1] : d[3];
-                if (sc) {
-                    g = g * sc[j];
-                    u = u * sc[p.ffn + j];
-                }
-                const float sig = 1.0f / (1.0f + expf(-g));
-                act[j] = (g * sig) * u;
-            }
+        const float v = chunk_dot<WT>(2 * n, p.hidden, [&](int r) {
+            return buf_ + (r & 1 ? c.off1 : 0) + (size_t)(r >> 1) * rb;
+        });
+        const float u = __shfl_down_sync(0xffffffffu, v, 1);
+        if (tid < 2 * n && (tid & 1) == 0) {
+            const int jj = tid >> 1, j = c.a + jj;
+            const float g = v * scale(isc, j - r0, p.ffn);
+            const float up = u * scale(isc, nrows + (j - r0), p.ffn);
+            const float sig = 1.0f / (1.0f + expf(-g));
+            ll_put(S.act + (size_t)c.l * p.ffn + j, (g * sig) * up, tag);
         }
     }
 
-    __device__ void rows_lm(const Chunk& c, const unsigned char* buf) {
+    __device__ void rows_lm(const Chunk& c, const unsigned char* buf_) {
         const int n = c.b - c.a;
         const size_t rb = (size_t)p.hidden;
-        for (int r0 = warp * 4; r0 < n; r0 += 4 * kCWarps) {
-            const unsigned char* rows[4] = {buf + (size_t)r0 * rb, buf + (size_t)(r0 + 1) * rb,
-                                            buf + (size_t)(r0 + 2) * rb, buf + (size_t)(r0 + 3) * rb};
-            float d[4];
-            const int nv = min(4, n - r0);
-            rows_dot<B2_W_I8, 4>(rows, nv, xs, p.hidden, lane, d);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                if (i >= nv) break;
-                const int r = c.a + r0 + i;
-                const float logit = d[i] * p.lm_s[r];
-                if (lane == i && p.logits) p.logits[r] = logit;
-                const unsigned long long k = b2::argmax_key(logit, (uint32_t)r);
-                best = k > best ? k : best;
-            }
+        const float v = chunk_dot<B2_W_I8>(n, p.hidden, [&](int r) { return buf_ + (size_t)r * rb; });
+        if (tid < n) {
+            const int r = c.a + tid;
+            const float logit = v * scale(isc, r - r0, 0);
+            if (p.logits) p.logits[r] = logit;
+            const unsigned long long k = b2::argmax_key(logit, (uint32_t)r);
+            best = k > best ? k : best;
         }
     }
 
     // ── attention: one (kv head g, position range) unit ──
 
     __device__ void attn_prologue(const Item& it) {
+        // The unit's softmax state starts here on every path, so it is dead
+        // (holds no registers) outside attention items.
+#pragma unroll
+        for (int h2 = 0; h2 < kMaxGq; h2++) {
+            m_[h2] = -INFINITY;
+            l_[h2] = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; j++) o_[h2][j] = qv_[h2][j] = 0.f;
+        }
         const int Gq = geo.Gq;
-        const float* qkv = S.qkv + (size_t)it.l * geo.nqkv;
+        const unsigned long long* qkv = S.qkv + (size_t)it.l * geo.nqkv;
         const B2MkLayer& Lw = p.layers[it.l];
         const int h = warp;  // warps 0..Gq-1: q heads, Gq: k head, Gq+1: v head
+        const int e0 = lane * 4;
+        bool ok = true;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        float nw[4] = {1.f, 1.f, 1.f, 1.f}, cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* nwp = h < Gq ? Lw.q_norm : h == Gq ? Lw.k_norm : nullptr;
         if (h <= Gq + 1) {
-            const int e0 = lane * 4;
-            const float* src = h < Gq ? qkv + (size_t)(it.g * Gq + h) * kHD
-                                      : h == Gq ? qkv + geo.qd + (size_t)it.g * kHD
-                                                : qkv + geo.qd + geo.kvd + (size_t)it.g * kHD;
-            float x[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) x[j] = __ldcg(src + e0 + j);
+            // static inputs first: their latency overlaps the poll below
+            if (nwp) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(nwp + e0));
+                nw[0] = t.x, nw[1] = t.y, nw[2] = t.z, nw[3] = t.w;
+            }
             if (h <= Gq) {
-                const float* nw = h < Gq ? Lw.q_norm : Lw.k_norm;
-                if (nw) {
+                const float* ct = p.cos_tab + (size_t)geo.pos * (kHD / 2);
+                const float* st = p.sin_tab + (size_t)geo.pos * (kHD / 2);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    // interleaved pairs (2i, 2i+1) use angle i; split halves (e, e + hd/2) use angle e
+                    const int i = p.rope_style == 0 ? (e0 + j) >> 1 : (lane < 16 ? e0 + j : e0 + j - kHD / 2);
+                    cs[j] = __ldg(ct + i);
+                    sn[j] = __ldg(st + i);
+                }
+            }
+            const unsigned long long* src = h < Gq ? qkv + (size_t)(it.g * Gq + h) * kHD
+                                            : h == Gq ? qkv + geo.qd + (size_t)it.g * kHD
+                                                      : qkv + geo.qd + geo.kvd + (size_t)it.g * kHD;
+            ok = warp_lead_wait(src, true);
+            for (long long t = 0; ok; t++) {
+                const ulonglong2 a = ll_get2(src + e0), b = ll_get2(src + e0 + 2);
+                if (ll_ok(a.x, tag) && ll_ok(a.y, tag) && ll_ok(b.x, tag) && ll_ok(b.y, tag)) {
+                    x[0] = ll_val(a.x), x[1] = ll_val(a.y), x[2] = ll_val(b.x), x[3] = ll_val(b.y);
+                    break;
+                }
+                if (t > kPollLimit || ((t & 63) == 63 && abort_seen())) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+        settle(ok);
+        if (stop()) return;
+        if (h <= Gq + 1) {
+            if (h <= Gq) {
+                if (nwp) {
                     float ss = 0.f;
 #pragma unroll
                     for (int j = 0; j < 4; j++) ss = fmaf(x[j], x[j], ss);
                     ss = b2::warp_sum(ss);
                     const float rms = 1.0f / sqrtf(ss / (float)kHD + p.eps);
 #pragma unroll
-                    for (int j = 0; j < 4; j++) x[j] = (x[j] * rms) * nw[e0 + j];
+                    for (int j = 0; j < 4; j++) x[j] = (x[j] * rms) * nw[j];
                 }
-                const float* cs = p.cos_tab + (size_t)geo.pos * (kHD / 2);
-                const float* sn = p.sin_tab + (size_t)geo.pos * (kHD / 2);
                 if (p.rope_style == 0) {
 #pragma unroll
                     for (int j = 0; j < 4; j += 2) {
-                        const int i = (e0 + j) >> 1;
                         const float x0 = x[j], x1 = x[j + 1];
-                        x[j] = x0 * cs[i] - x1 * sn[i];
-                        x[j + 1] = x1 * cs[i] + x0 * sn[i];
+                        x[j] = x0 * cs[j] - x1 * sn[j];
+                        x[j + 1] = x1 * cs[j] + x0 * sn[j];
                     }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         const float other = __shfl_xor_sync(0xffffffffu, x[j], 16);
-                        const int e = e0 + j;
-                        const int i = lane < 16 ? e : e - kHD / 2;
-                        const float c0 = cs[i], s0 = sn[i];
-                        x[j] = lane < 16 ? x[j] * c0 - other * s0 : x[j] * c0 + other * s0;
+                        x[j] = lane < 16 ? x[j] * cs[j] - other * sn[j] : x[j] * cs[j] + other * sn[j];
                     }
                 }
             }
@@ -777,15 +1008,9 @@ struct Consumer {
         consumer_sync();
         const int sub = lane & 7;
 #pragma unroll
-        for (int h2 = 0; h2 < kMaxGq; h2++) {
-            m_[h2] = -INFINITY;
-            l_[h2] = 0.f;
+        for (int h2 = 0; h2 < kMaxGq; h2++)
 #pragma unroll
-            for (int j = 0; j < 16; j++) {
-                o_[h2][j] = 0.f;
-                qv_[h2][j] = h2 < Gq ? sh.q[h2][sub * 16 + j] : 0.f;
-            }
-        }
+            for (int j = 0; j < 16; j++) qv_[h2][j] = h2 < Gq ? sh.q[h2][sub * 16 + j] : 0.f;
     }
 
     // One position per lane group; kf/vf are this lane's 16 dims.
@@ -901,46 +1126,12 @@ struct Consumer {
                     ls = fmaf(sh.gl[r][h], w, ls);
                     acc = fmaf(sh.go[r][h][d], w, acc);
                 }
-            float* part = S.part + (unit + h) * (2 + kHD);
-            part[2 + d] = acc;
+            unsigned long long* rec = S.part + (unit + h) * (2 + kHD);
+            ll_put(rec + 2 + d, acc, tag);
             if (d == 0) {
-                part[0] = M;
-                part[1] = ls;
+                ll_put(rec, M, tag);
+                ll_put(rec + 1, ls, tag);
             }
-        }
-        consumer_sync();
-        if (tid == 0) {
-            __threadfence();
-            const unsigned long long old = atom_add_acqrel(cnt(it.l, C_ATTN + it.g), 1ull);
-            sh.last = old == (unsigned long long)(geo.S - 1) ? 1 : 0;
-            __threadfence();
-        }
-        consumer_sync();
-        if (!sh.last) return;
-        // last unit of kv head g: merge the S position ranges of its q heads
-        for (int t = tid; t < Gq * kHD; t += kConsumers) {
-            const int h = t / kHD, d = t % kHD;
-            float M = -INFINITY;
-            for (int s = 0; s < geo.S; s++) {
-                const float* part = S.part + ((((size_t)it.l * p.nkv + it.g) * kMaxSplit + s) * Gq + h) * (2 + kHD);
-                M = fmaxf(M, __ldcg(part));
-            }
-            float num = 0.f, den = 0.f;
-            for (int s = 0; s < geo.S; s++) {
-                const float* part = S.part + ((((size_t)it.l * p.nkv + it.g) * kMaxSplit + s) * Gq + h) * (2 + kHD);
-                const float ms = __ldcg(part);
-                if (ms == -INFINITY) continue;
-                const float w = expf(ms - M);
-                den = fmaf(__ldcg(part + 1), w, den);
-                num = fmaf(__ldcg(part + 2 + d), w, num);
-            }
-            S.attn[(size_t)it.l * geo.qd + (size_t)(it.g * Gq + h) * kHD + d] = num / den;
-        }
-        consumer_sync();
-        if (tid == 0) {
-            *(volatile unsigned long long*)cnt(it.l, C_ATTN + it.g) = 0ull;  // reset for the next step
-            __threadfence();
-            red_release(cnt(it.l, C_ATTN_DONE), 1ull);
         }
     }
 };
@@ -977,7 +1168,8 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
     geo.nqkv = geo.qd + 2 * geo.kvd;
     geo.Gq = p.nq / p.nkv;
     {
-        int s = (geo.L + 63) / 64;
+        // one position range per 256 cached positions, at most one unit per CTA
+        int s = (geo.L + 255) / 256;
         const int cap = min(kMaxSplit, max(1, geo.G / p.nkv));
         geo.S = max(1, min(s, cap));
     }
@@ -991,12 +1183,12 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
     } else {
         const int tok = p.state[B2_MK_TOKEN];
         const float* emb_row = p.state[B2_MK_USE_EMB] ? p.staged_emb : p.emb + (size_t)tok * p.hidden;
-        Consumer<WT> cons{p, geo, sh, ring, xs, S, gen + 1, emb_row, tid, lane, warp};
+        Consumer<WT> cons{p, geo, sh, ring, xs, S, (uint32_t)(gen + 1), emb_row, tid, lane, warp};
         walk<WT>(p, geo, cons);
         if (!cons.stop()) {  // FIN: the last CTA publishes the step
             consumer_sync();
             if (tid == 0) {
-                unsigned long long* fin = S.cnt + (size_t)p.n_layers * kCntPerLayer;
+                unsigned long long* fin = S.cnt;
                 __threadfence();
                 const unsigned long long old = atom_add_acqrel(fin, 1ull);
                 if (old == (unsigned long long)(geo.G - 1)) {
@@ -1035,6 +1227,7 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
 }
 
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kMaxK * sizeof(__half) + sizeof(Shared) + 128;
+static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB per-block limit");
 
 template <int WT>
 int launch(const B2MkPlan* p, cudaStream_t s) {
@@ -1070,7 +1263,7 @@ int launch(const B2MkPlan* p, cudaStream_t s) {
 
 extern "C" float* b2_mk_final_hidden(const B2MkPlan* p) {
     Scratch s = scratch_layout(p->scratch, p->n_layers, p->hidden, p->ffn, p->nq, p->nkv, p->hd, nullptr);
-    return s.hbuf + (size_t)p->n_layers * p->hidden;
+    return s.hfinal;
 }
 
 extern "C" size_t b2_mk_smem_bytes(void) { return kSmemBytes; }
@@ -1086,9 +1279,11 @@ extern "C" int b2_mk_check(const B2MkPlan* p) {
     if (p->n_layers < 1 || p->n_layers > B2_MK_MAX_LAYERS || p->hd != kHD || p->nkv < 1 || p->nkv > 8 ||
         p->nq % p->nkv != 0 || p->nq / p->nkv > kMaxGq)
         return B2_ERR_INVALID_ARG;
-    const int E = p->wtype == B2_W_F16 ? 8 : p->wtype == B2_W_I8 ? 16 : 32;
-    if (p->hidden % E || p->ffn % E || (p->nq * kHD) % E || p->hidden > kMaxK || p->ffn > kMaxK ||
-        p->nq * kHD > kMaxK || p->hidden % 16)
+    // K of every matmul: a whole number of 64-byte super-blocks (the int8
+    // lm_head included), and short enough to stage
+    const int E = p->wtype == B2_W_F16 ? 32 : p->wtype == B2_W_I8 ? 64 : 128;
+    if (p->hidden % E || p->ffn % E || (p->nq * kHD) % E || p->hidden % 64 || p->hidden > kMaxK ||
+        p->ffn > kMaxK || p->nq * kHD > kMaxK)
         return B2_ERR_INVALID_ARG;
     // every streamed row range must fit one stage at least one row at a time
     if (2 * row_bytes(p->wtype, p->hidden) > (size_t)kStageBytes || row_bytes(p->wtype, p->ffn) > (size_t)kStageBytes ||

@@ -39,50 +39,24 @@ struct WTraits<B2_W_I4> {
     static constexpr int kRows = 4;
 };
 
-// acc += sum over the 8 elements of one 16-byte activation chunk times w[8].
-__device__ __forceinline__ float dot8(const uint4 xv, const float (&w)[8], float acc) {
-    float2 x0 = b2::h2_to_f2(xv.x), x1 = b2::h2_to_f2(xv.y);
-    float2 x2 = b2::h2_to_f2(xv.z), x3 = b2::h2_to_f2(xv.w);
+// acc += sum over 8 staged activations x[0..8) times w[8].
+__device__ __forceinline__ float dot8(const float4 x0, const float4 x1, const float (&w)[8], float acc) {
     acc = fmaf(x0.x, w[0], acc);
     acc = fmaf(x0.y, w[1], acc);
-    acc = fmaf(x1.x, w[2], acc);
-    acc = fmaf(x1.y, w[3], acc);
-    acc = fmaf(x2.x, w[4], acc);
-    acc = fmaf(x2.y, w[5], acc);
-    acc = fmaf(x3.x, w[6], acc);
-    acc = fmaf(x3.y, w[7], acc);
+    acc = fmaf(x0.z, w[2], acc);
+    acc = fmaf(x0.w, w[3], acc);
+    acc = fmaf(x1.x, w[4], acc);
+    acc = fmaf(x1.y, w[5], acc);
+    acc = fmaf(x1.z, w[6], acc);
+    acc = fmaf(x1.w, w[7], acc);
     return acc;
-}
-
-// Expand 8 consecutive weights (group g of the 16-byte chunk) to FP32.
-template <int WT>
-__device__ __forceinline__ void expand8(const uint4 wv, int g, float (&w)[8]) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&wv);
-    if constexpr (WT == B2_W_F16) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float2 f = b2::h2_to_f2(u[i]);
-            w[2 * i] = f.x;
-            w[2 * i + 1] = f.y;
-        }
-    } else if constexpr (WT == B2_W_I8) {
-        uint32_t a = u[2 * g], b = u[2 * g + 1];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            w[i] = (float)(int8_t)(a >> (8 * i));
-            w[4 + i] = (float)(int8_t)(b >> (8 * i));
-        }
-    } else {  // int4: word g holds 8 nibbles, element i at bits [4i, 4i+4)
-        uint32_t a = u[g];
-#pragma unroll
-        for (int i = 0; i < 8; i++) w[i] = (float)(((int32_t)(a << (28 - 4 * i))) >> 28);
-    }
 }
 
 template <int WT, int MR, bool PAIR>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(B2GemvArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);  // [MR][K]
+    // [MR][K] activations, FP16-rounded, held as FP32 times x_scale<WT>()
+    float* xs = reinterpret_cast<float*>(smem);
     __shared__ float red[kWarps][MR];
     const int K = a.K;
     const int m0 = blockIdx.y * MR;
@@ -104,7 +78,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(B2GemvArgs a) {
     b2::pdl_trigger();
     b2::pdl_wait();
 
-    // ── prologue: activation rows -> (optional RMSNorm) -> FP16 in smem ──
+    // ── prologue: activation rows -> (optional RMSNorm) -> FP16 rounding -> smem ──
     float rms[MR];
     if (a.norm_w) {
         float ss[MR];
@@ -134,7 +108,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(B2GemvArgs a) {
         for (int k = tid; k < K; k += kThreads) {
             float v = live ? xr[k] : 0.f;
             if (a.norm_w) v = (v * rms[r]) * a.norm_w[k];
-            xs[r * K + k] = __float2half_rn(v);
+            xs[r * K + k] = __half2float(__float2half_rn(v)) * b2::x_scale<WT>();
         }
     }
     __syncthreads();
@@ -177,16 +151,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(B2GemvArgs a) {
             if (c >= nchunks) break;
 #pragma unroll
             for (int g = 0; g < E / 8; g++) {
-                uint4 xv[MR];
+                float w[RR][8];
 #pragma unroll
-                for (int r = 0; r < MR; r++)
-                    xv[r] = *reinterpret_cast<const uint4*>(xs + r * K + c * E + g * 8);
+                for (int j = 0; j < RR; j++) b2::expand8_exact<WT>(wv[j][u], g, w[j]);
 #pragma unroll
-                for (int j = 0; j < RR; j++) {
-                    float w[8];
-                    expand8<WT>(wv[j][u], g, w);
+                for (int r = 0; r < MR; r++) {
+                    const float4* xp = reinterpret_cast<const float4*>(xs + r * K + c * E + g * 8);
+                    const float4 x0 = xp[0], x1 = xp[1];
 #pragma unroll
-                    for (int r = 0; r < MR; r++) acc[j][r] = dot8(xv[r], w, acc[j][r]);
+                    for (int j = 0; j < RR; j++) acc[j][r] = dot8(x0, x1, w[j], acc[j][r]);
                 }
             }
         }
@@ -225,7 +198,7 @@ template <int WT, int MR, bool PAIR>
 int launch(const B2GemvArgs* a, cudaStream_t s) {
     constexpr int R = WTraits<WT>::kRows;
     dim3 grid((a->N + kWarps * R - 1) / (kWarps * R), (a->M + MR - 1) / MR);
-    size_t smem = (size_t)MR * a->K * sizeof(__half);
+    size_t smem = (size_t)MR * a->K * sizeof(float);
     auto fn = gemv_kernel<WT, MR, PAIR>;
     if (smem + 2048 > 48 * 1024) {  // static shared memory counts against the same limit
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

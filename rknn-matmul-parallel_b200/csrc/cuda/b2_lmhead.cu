@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(kThreads) lm_head_kernel(const float* __restri
                 float w[E];
                 const uint32_t* wu = &wv[j][u].x;
                 if constexpr (WT == B2_W_I8) {
-#pragma unroll
-                    for (int i = 0; i < 16; i++) w[i] = (float)(int8_t)(wu[i >> 2] >> (8 * (i & 3)));
+                    b2::expand8_exact<B2_W_I8>(wv[j][u], 0, *reinterpret_cast<float(*)[8]>(w));
+                    b2::expand8_exact<B2_W_I8>(wv[j][u], 1, *reinterpret_cast<float(*)[8]>(w + 8));
                 } else if constexpr (WT == B2_W_F16) {
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
