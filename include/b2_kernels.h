@@ -103,6 +103,35 @@ typedef struct {
 } B2GemvArgs;
 int b2_gemv(const B2GemvArgs* a, b2_stream_t s);
 
+/* Rows to FP16 for the tensor-core GEMM: y16[m][k] = f16(xn[m][k]) for
+ * m < M, with xn = x or RMSNorm(x; norm_w, eps) exactly as in b2_gemv's
+ * prologue.  y16 is device FP16 (uint16_t bits) with row stride ldy
+ * (elements, a multiple of 8). */
+int b2_rows_to_f16(uint16_t* y16, int ldy, const float* x, int ldx, int M, int K, const float* norm_w,
+                   float eps, b2_stream_t s);
+
+/* Tensor-core GEMM for M > 1 (batch prefill), FP16 weights:
+ * y[m][n] = epi( s[n] * sum_k x16[m][k] * W[n][k] ) with the epilogues of
+ * b2_gemv (SILU_PAIR: rows n and N+n).  x16 comes from b2_rows_to_f16;
+ * the sum runs on the 5th-generation tensor cores (tcgen05.mma, FP16
+ * operands staged by TMA, FP32 accumulator in tensor memory), so the
+ * numerics equal b2_gemv's up to the FP32 summation order.  Shapes: K a
+ * multiple of 64, N a multiple of 128 (of 64 for SILU_PAIR), ldx a multiple
+ * of 8; x16 and W 16-byte aligned.  Same role as b2_gemv in the reference
+ * map (run_batch_matmul, src/matmul_decoder.c:1841-1899). */
+typedef struct {
+    float* y;
+    int ldy;
+    const uint16_t* x16;
+    int ldx;
+    int M, K, N;
+    const void* w;
+    const float* scales;
+    int wtype; /* B2_W_F16 */
+    int epilogue;
+} B2GemmArgs;
+int b2_gemm(const B2GemmArgs* a, b2_stream_t s);
+
 /* Embedding: for row m, hidden[m] = use_staged && *use_staged ? staged[m]
  * : table[tokens[m]].  tokens, use_staged, staged are device pointers
  * (use_staged/staged may be NULL). */

@@ -1,0 +1,368 @@
+// Tensor-core GEMM for M > 1 rows (batch prefill): b2_gemm, b2_rows_to_f16.
+//
+// Same contract as b2_gemv (the reference's run_batch_matmul,
+// src/matmul_decoder.c:1841-1899: FP16-rounded activations, FP16 weights,
+// FP32 accumulation, per-column scale, then the residual add or SiLU*mul of
+// src/cpu_ops.c:296-319, :350-359), but the sums run on the sm_100 tensor
+// cores:
+//
+//   warp 0       one thread issues TMA tile loads (cp.async.bulk.tensor, 128-byte
+//                swizzle) of a 128-row weight tile and a BN-row activation tile
+//                per 64-wide k step into a 4-stage shared-memory ring;
+//   warp 1       allocates the tensor-memory accumulator (128 lanes x BN FP32
+//                columns) and one thread issues tcgen05.mma (M=128, N=BN, K=16,
+//                FP16 x FP16 -> FP32), committing each stage back to the loader;
+//   warps 2-5    read the accumulator with tcgen05.ld (warp w owns lanes
+//                32*(w%4)..+31, i.e. 32 output columns) and apply the epilogue.
+//
+// The weight tile is the MMA's A operand (output columns are TMEM lanes) and
+// the activation tile its B operand (token rows are TMEM columns), so one
+// CTA computes a 128-column x BN-row block of y.  For SILU_PAIR the A tile is
+// 64 gate rows followed by the 64 matching up rows; the up half crosses to
+// the gate half through shared memory in the epilogue.
+#include <cuda.h>  // CUtensorMap and its enums; the encoder is looked up at run time
+
+#include <mutex>
+
+#include "b2_common.cuh"
+
+namespace {
+
+constexpr int kBM = 128;     // weight rows per tile (MMA M)
+constexpr int kBK = 64;      // k per stage: 64 FP16 = one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr long long kWaitLimit = 1ll << 22;
+
+struct GemmParams {
+    float* y;
+    int ldy;
+    int M, K, N;
+    const float* scales;
+    int epilogue;
+};
+
+struct Bars {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t done;
+    uint32_t tmem;
+    int failed;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false (and the CTA's failure flag) after kWaitLimit polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Bars* b) {
+    for (long long it = 0; !mbar_try_wait(bar, parity); it++) {
+        if (it > kWaitLimit || *(volatile int*)&b->failed) {
+            b->failed = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile stored as 128-byte rows
+// with the 128-byte swizzle (8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4)  // start address
+           | ((uint64_t)1 << 16)                // leading byte offset (fixed for swizzled K-major)
+           | ((uint64_t)(1024 >> 4) << 32)      // stride byte offset: one 8-row group
+           | ((uint64_t)1 << 46)                // descriptor version
+           | ((uint64_t)2 << 61);               // 128-byte swizzle
+}
+
+// Instruction descriptor of kind::f16: FP16 A and B (both K-major), FP32 D.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, bool PAIR>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const GemmParams g) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    constexpr int kABytes = kBM * 128, kBBytes = BN * 128, kStage = kABytes + kBBytes;
+    Bars* b = reinterpret_cast<Bars*>(smem + kStages * kStage);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BN;
+    const int KT = g.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&b->full[s], 1);
+            mbar_init(&b->empty[s], 1);
+        }
+        mbar_init(&b->done, 1);
+        b->failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tw) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
+    }
+    if (warp == 1) {  // accumulator: 128 lanes x BN FP32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&b->tmem)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = b->tmem;
+    // The activation rows come from the previous kernel of the stream.
+    b2::pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            for (int kt = 0; kt < KT; kt++) {
+                const int s = kt % kStages;
+                if (kt >= kStages && !mbar_wait(&b->empty[s], (uint32_t)((kt / kStages - 1) & 1), b)) break;
+                unsigned char* sa = smem + s * kStage;
+                mbar_expect_tx(&b->full[s], kStage);
+                if (PAIR) {
+                    tma_load_2d(sa, &tw, kt * kBK, 64 * blockIdx.x, &b->full[s]);
+                    tma_load_2d(sa + 64 * 128, &tw, kt * kBK, g.N + 64 * blockIdx.x, &b->full[s]);
+                } else {
+                    tma_load_2d(sa, &tw, kt * kBK, kBM * blockIdx.x, &b->full[s]);
+                }
+                tma_load_2d(sa + kABytes, &tx, kt * kBK, m0, &b->full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_f16(kBM, BN);
+            for (int kt = 0; kt < KT; kt++) {
+                const int s = kt % kStages;
+                if (!mbar_wait(&b->full[s], (uint32_t)((kt / kStages) & 1), b)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * kStage), sb = sa + kABytes;
+#pragma unroll
+                for (int k = 0; k < kBK / 16; k++)  // K = 16 per MMA: 32 bytes along the swizzled row
+                    umma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (kt | k) != 0);
+                umma_commit(&b->empty[s]);
+            }
+            umma_commit(&b->done);
+        }
+    } else {  // epilogue warps 2..5
+        const int quad = warp & 3;  // TMEM lanes this warp may read
+        const bool ok = mbar_wait(&b->done, 0, b);
+        tc_fence_after();
+        if (!PAIR) {
+            const int n = kBM * blockIdx.x + 32 * quad + lane;
+            const float sc = g.scales ? g.scales[n] : 1.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN && ok; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int m = m0 + c0 + j;
+                    if (m >= g.M) break;
+                    float* yp = g.y + (size_t)m * g.ldy + n;
+                    const float val = __uint_as_float(v[j]) * sc;
+                    *yp = g.epilogue == B2_EPI_ADD ? *yp + val : val;
+                }
+            }
+        } else {
+            // lanes 0-63: gate rows of channels ch0..ch0+63, lanes 64-127: the up rows
+            float* xch = reinterpret_cast<float*>(smem);  // [64][17]; the stage ring is idle now
+            const int ch = 64 * blockIdx.x + 32 * (quad & 1) + lane;
+            const bool up = quad >= 2;
+            const float sc = g.scales ? g.scales[up ? g.N + ch : ch] : 1.f;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                if (ok) tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
+                if (up)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) xch[(32 * (quad & 1) + lane) * 17 + j] = __uint_as_float(v[j]) * sc;
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (!up && ok) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int m = m0 + c0 + j;
+                        if (m >= g.M) break;
+                        const float gv = __uint_as_float(v[j]) * sc;
+                        const float uv = xch[(32 * quad + lane) * 17 + j];
+                        const float sig = 1.0f / (1.0f + expf(-gv));
+                        g.y[(size_t)m * g.ldy + ch] = (gv * sig) * uv;
+                    }
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+        }
+    }
+    b2::pdl_trigger();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    }
+}
+
+// ── b2_rows_to_f16: one CTA per row ──
+__global__ void __launch_bounds__(256) rows_to_f16_kernel(uint16_t* __restrict__ y16, int ldy,
+                                                         const float* __restrict__ x, int ldx, int K,
+                                                         const float* __restrict__ norm_w, float eps) {
+    __shared__ float red[8];
+    b2::pdl_wait();
+    const float* xr = x + (size_t)blockIdx.x * ldx;
+    __half* yr = reinterpret_cast<__half*>(y16) + (size_t)blockIdx.x * ldy;
+    const int tid = threadIdx.x;
+    float rms = 1.f;
+    if (norm_w) {
+        float ss = 0.f;
+        for (int k = tid; k < K; k += 256) ss = fmaf(xr[k], xr[k], ss);
+        ss = b2::warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) t += red[w];
+        rms = 1.0f / sqrtf(t / (float)K + eps);
+    }
+    for (int k = tid; k < K; k += 256) {
+        float v = xr[k];
+        if (norm_w) v = (v * rms) * norm_w[k];
+        yr[k] = __float2half_rn(v);
+    }
+    b2::pdl_trigger();
+}
+
+// ── host side ──
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 2-D FP16 tensor [outer][inner] with rows row_bytes apart, loaded in boxes of
+// box_outer rows x 64 elements with the 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+             uint32_t box_outer) {
+    EncodeTiledFn enc = encoder();
+    if (!enc) return b2_set_error(B2_ERR_CUDA, "b2_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, box_outer};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return b2_set_error(B2_ERR_CUDA, "b2_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+template <int BN, bool PAIR>
+int launch(const B2GemmArgs* a, cudaStream_t s) {
+    CUtensorMap tw, tx;
+    int rc = make_map(&tw, a->w, (uint64_t)a->K, (uint64_t)(PAIR ? 2 * a->N : a->N), (uint64_t)a->K * 2,
+                      PAIR ? 64 : kBM);
+    if (!rc) rc = make_map(&tx, a->x16, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->ldx * 2, BN);
+    if (rc) return rc;
+    constexpr size_t smem = (size_t)kStages * (kBM * 128 + BN * 128) + sizeof(Bars) + 1024;
+    auto fn = gemm_kernel<BN, PAIR>;
+    static std::once_flag once[8];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = cudaSuccess;
+    std::call_once(once[dev & 7], [&] { e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm smem attr: %s", cudaGetErrorString(e));
+    GemmParams g{a->y, a->ldy, a->M, a->K, a->N, a->scales, a->epilogue};
+    const dim3 grid(PAIR ? a->N / 64 : a->N / kBM, (a->M + BN - 1) / BN);
+    e = b2::launch_pdl(fn, grid, dim3(kThreads), smem, s, tw, tx, g);
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm launch: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int b2_gemm(const B2GemmArgs* a, b2_stream_t stream) {
+    if (!a || !a->y || !a->x16 || !a->w || a->M < 0 || a->K <= 0 || a->N <= 0)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_gemm: bad arguments");
+    if (a->M == 0) return 0;
+    const bool pair = a->epilogue == B2_EPI_SILU_PAIR;
+    if (a->wtype != B2_W_F16 || a->K % kBK || a->N % (pair ? 64 : kBM) || a->ldx % 8 || a->ldx < a->K ||
+        a->ldy < (pair ? a->N : a->N) || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
+        (reinterpret_cast<uintptr_t>(a->w) & 15))
+        return b2_set_error(B2_ERR_INVALID_ARG,
+                            "b2_gemm: needs FP16 weights, K %% 64 == 0, N %% %d == 0, ldx %% 8 == 0, aligned operands",
+                            pair ? 64 : kBM);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (a->M <= 64) return pair ? launch<64, true>(a, s) : launch<64, false>(a, s);
+    return pair ? launch<128, true>(a, s) : launch<128, false>(a, s);
+}
+
+extern "C" int b2_rows_to_f16(uint16_t* y16, int ldy, const float* x, int ldx, int M, int K, const float* norm_w,
+                              float eps, b2_stream_t stream) {
+    if (!y16 || !x || M < 0 || K <= 0 || ldy < K || ldx < K || ldy % 8)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_rows_to_f16: bad arguments");
+    if (M == 0) return 0;
+    cudaError_t e = b2::launch_pdl(rows_to_f16_kernel, dim3(M), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                                   y16, ldy, x, ldx, K, norm_w, eps);
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_rows_to_f16 launch: %s", cudaGetErrorString(e));
+    return 0;
+}

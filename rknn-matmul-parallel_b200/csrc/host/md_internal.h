@@ -94,6 +94,7 @@ typedef struct {
     float* act;      /* [M][ffn] */
     void* attn_work;
     int attn_split;
+    uint16_t* x16;   /* [M][max(H, qd, ffn)] FP16 staging for the tensor-core GEMM, or NULL */
 } LayerBuffers;
 int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2KVRef* kv_proto,
                       b2_stream_t s);

@@ -11,14 +11,44 @@
  *   4. o_proj GEMV + residual add into hidden                       (b2_gemv ADD)
  *   5. RMSNorm(post_attn_norm) + gate|up GEMV + SiLU*mul            (b2_gemv SILU_PAIR)
  *   6. down GEMV + residual add into hidden                         (b2_gemv ADD)
+ * With M >= MD_GEMM_MIN_ROWS rows and FP16 weights, steps 1, 4, 5 and 6 run
+ * as b2_rows_to_f16 (RMSNorm + FP16 rounding) + b2_gemm (tcgen05 tensor cores).
  * K/V of the current rows are stored before attention for decode and
  * prefill alike; the reference stores them after attention in prefill
  * (:2026-2034) but reads the same values from its batch buffers, so the
  * attended set is identical.
  */
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "md_internal.h"
+
+/* Rows from which a matmul runs on the tensor cores (b2_rows_to_f16 +
+ * b2_gemm) instead of the GEMV; B2_PREFILL_GEMM=0 keeps every M on the GEMV. */
+#define MD_GEMM_MIN_ROWS 16
+
+static int gemm_enabled(void) {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("B2_PREFILL_GEMM");
+        v = !(e && e[0] == '0');
+    }
+    return v;
+}
+
+/* One matmul of the layer: the GEMV, or for M >= MD_GEMM_MIN_ROWS rows of
+ * FP16 weights the same operation on the tensor cores. */
+static int linear(const LayerBuffers* b, const B2GemvArgs* a, b2_stream_t s) {
+    const int pair = a->epilogue == B2_EPI_SILU_PAIR;
+    if (b->x16 && a->M >= MD_GEMM_MIN_ROWS && a->wtype == B2_W_F16 && a->K % 64 == 0 &&
+        a->N % (pair ? 64 : 128) == 0 && gemm_enabled()) {
+        int rc = b2_rows_to_f16(b->x16, a->K, a->x, a->ldx, a->M, a->K, a->norm_w, a->eps, s);
+        if (rc) return rc;
+        B2GemmArgs g = {a->y, a->ldy, b->x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype, a->epilogue};
+        return b2_gemm(&g, s);
+    }
+    return b2_gemv(a, s);
+}
 
 int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2KVRef* kv_proto,
                       b2_stream_t s) {
@@ -29,7 +59,7 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         const DevLayer* L = &m->layers[l];
         B2GemvArgs a = {b->qkv, ldqkv, b->hidden, H, M, H, ldqkv, L->qkv.w, L->qkv.s, L->qkv.wtype,
                         L->in_norm, c->rms_eps, B2_EPI_STORE};
-        int rc = b2_gemv(&a, s);
+        int rc = linear(b, &a, s);
         if (rc) return rc;
         B2KVRef kv = *kv_proto;
         kv.layer = l;
@@ -41,15 +71,15 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         if (rc) return rc;
         B2GemvArgs o = {b->hidden, H, b->attn, qd, M, qd, H, L->o.w, L->o.s, L->o.wtype, NULL, 0.f,
                         B2_EPI_ADD};
-        rc = b2_gemv(&o, s);
+        rc = linear(b, &o, s);
         if (rc) return rc;
         B2GemvArgs gu = {b->act, F, b->hidden, H, M, H, F, L->gu.w, L->gu.s, L->gu.wtype, L->post_norm,
                          c->rms_eps, B2_EPI_SILU_PAIR};
-        rc = b2_gemv(&gu, s);
+        rc = linear(b, &gu, s);
         if (rc) return rc;
         B2GemvArgs dn = {b->hidden, H, b->act, F, M, F, H, L->down.w, L->down.s, L->down.wtype, NULL, 0.f,
                          B2_EPI_ADD};
-        rc = b2_gemv(&dn, s);
+        rc = linear(b, &dn, s);
         if (rc) return rc;
     }
     return 0;

@@ -48,6 +48,12 @@ class B2GemvArgs(ctypes.Structure):
                 ("norm_w", c_vp), ("eps", c_float), ("epilogue", c_int)]
 
 
+class B2GemmArgs(ctypes.Structure):
+    _fields_ = [("y", c_vp), ("ldy", c_int), ("x16", c_vp), ("ldx", c_int), ("M", c_int),
+                ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
+                ("epilogue", c_int)]
+
+
 class B2KVRef(ctypes.Structure):
     _fields_ = [("k_base", c_vp), ("v_base", c_vp), ("seq_stride", ctypes.c_longlong),
                 ("layer_stride", ctypes.c_longlong), ("layer", c_int), ("max_seq", c_int),
@@ -119,6 +125,8 @@ SIGNATURES = {
     "b2_graph_launch": (c_int, [c_vp, c_vp]),
     "b2_graph_destroy": (c_int, [c_vp]),
     "b2_gemv": (c_int, [c_vp, c_vp]),
+    "b2_gemm": (c_int, [c_vp, c_vp]),
+    "b2_rows_to_f16": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_int, c_vp, c_float, c_vp]),
     "b2_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "b2_qk_rope_kv": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,
                               c_vp, c_vp, c_int, c_vp, c_vp]),

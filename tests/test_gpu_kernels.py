@@ -139,6 +139,108 @@ def test_gemv_silu_pair(wtype, M):
     assert_close(y_d.cpu().numpy(), exp)
 
 
+# ── tensor-core GEMM (batch prefill) ──
+
+def rows_f16(x_d, M, K, norm_w=None):
+    """b2_rows_to_f16 of device rows x_d [M, K] -> device FP16 [M, K]."""
+    y16 = torch.empty((M, K), dtype=torch.float16, device=DEV)
+    _LIVE.append(y16)
+    nw = dev(norm_w) if norm_w is not None else None
+    bd.check(bd.capi().b2_rows_to_f16(y16.data_ptr(), K, x_d.data_ptr(), K, M, K,
+                                      nw.data_ptr() if nw is not None else None, 1e-6, stream()),
+             "b2_rows_to_f16")
+    return y16
+
+
+def test_rows_to_f16_matches_oracle_rounding():
+    rng = np.random.default_rng(4242)
+    M, K = 37, 3072
+    x = rng.standard_normal((M, K), dtype=np.float32) * 3
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    got = rows_f16(dev(x), M, K, norm_w).cpu().numpy().astype(np.float32)
+    exp = np.stack([ref.rms_norm(r, norm_w) for r in x]).astype(np.float16).astype(np.float32)
+    # the device RMS sum runs in another order: an element may land on the
+    # neighbouring FP16 value, never further
+    ulp = np.abs(np.spacing(exp.astype(np.float16)).astype(np.float32))
+    assert np.all(np.abs(got - exp) <= ulp)
+    assert np.mean(got == exp) > 0.99
+    plain = rows_f16(dev(x), M, K).cpu().numpy()
+    np.testing.assert_array_equal(plain, x.astype(np.float16))
+
+
+def gemm_ref(x, w16, norm_w=None):
+    """FP32 reference of the GEMM numerics: FP16-rounded activations times FP16
+    weights, summed in FP32 (numpy BLAS)."""
+    xn = np.stack([ref.rms_norm(r, norm_w) for r in x]) if norm_w is not None else x
+    return xn.astype(np.float16).astype(np.float32) @ w16.astype(np.float32)
+
+
+@pytest.mark.parametrize("M", [16, 60, 130, 512])
+@pytest.mark.parametrize("KN", [(1024, 4096), (2048, 1024), (3072, 1024)])
+def test_gemm_tensor_cores_store_and_add(M, KN):
+    K, N = KN
+    rng = np.random.default_rng(5000 + M + K // 1024)
+    w16 = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    y0 = rng.standard_normal((M, N), dtype=np.float32)
+    w_d, x_d = dev(np.ascontiguousarray(w16.T)), dev(x)
+    for norm, epi in ((True, bd.EPI_STORE), (False, bd.EPI_ADD)):
+        exp = gemm_ref(x, w16, norm_w if norm else None) + (y0 if epi == bd.EPI_ADD else 0)
+        x16 = rows_f16(x_d, M, K, norm_w if norm else None)
+        y_d = dev(y0.copy())
+        a = bd.B2GemmArgs(y_d.data_ptr(), N, x16.data_ptr(), K, M, K, N, w_d.data_ptr(), None, bd.W_F16, epi)
+        bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm")
+        torch.cuda.synchronize()
+        assert_close(y_d.cpu().numpy(), exp)
+
+
+def test_gemm_tensor_cores_matches_oracle():
+    """One prefill-shaped case against the C oracle's reference matmul."""
+    M, K, N = 60, 1024, 1024
+    rng = np.random.default_rng(777)
+    w16 = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    exp = ref.gemm(x, w16, None, wtype=ref.W_F16, n=N)
+    x16 = rows_f16(dev(x), M, K)
+    y_d = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    w_d = dev(np.ascontiguousarray(w16.T))
+    a = bd.B2GemmArgs(y_d.data_ptr(), N, x16.data_ptr(), K, M, K, N, w_d.data_ptr(), None, bd.W_F16,
+                      bd.EPI_STORE)
+    bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm")
+    torch.cuda.synchronize()
+    assert_close(y_d.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("M", [16, 60, 512])
+def test_gemm_tensor_cores_silu_pair(M):
+    K, F = 1024, 3072
+    rng = np.random.default_rng(900 + M)
+    wg = (rng.standard_normal((K, F)) * 0.02).astype(np.float16)
+    wu = (rng.standard_normal((K, F)) * 0.02).astype(np.float16)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    g, u = gemm_ref(x, wg, norm_w), gemm_ref(x, wu, norm_w)
+    exp = g / (1 + np.exp(-g)) * u
+    rows = np.concatenate([np.ascontiguousarray(wg.T), np.ascontiguousarray(wu.T)])
+    x16 = rows_f16(dev(x), M, K, norm_w)
+    y_d = torch.zeros((M, F), dtype=torch.float32, device=DEV)
+    a = bd.B2GemmArgs(y_d.data_ptr(), F, x16.data_ptr(), K, M, K, F, dev(rows).data_ptr(), None, bd.W_F16,
+                      bd.EPI_SILU_PAIR)
+    bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm pair")
+    torch.cuda.synchronize()
+    assert_close(y_d.cpu().numpy(), exp)
+
+
+def test_gemm_rejects_unsupported_shapes():
+    a = bd.B2GemmArgs(16, 128, 16, 100, 32, 100, 128, 16, None, bd.W_F16, 0)   # K % 64
+    assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
+    a = bd.B2GemmArgs(16, 128, 16, 128, 32, 128, 128, 16, None, bd.W_I8, 0)    # quantized weights
+    assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
+    a = bd.B2GemmArgs(16, 96, 16, 128, 32, 128, 96, 16, None, bd.W_F16, 0)     # N % 128
+    assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
+
+
 def test_gemv_rejects_bad_shapes():
     a = bd.B2GemvArgs(1, 8, 1, 8, 1, 1000, 8, 16, None, bd.W_I4, None, 0.0, 0)
     assert bd.capi().b2_gemv(ctypes.byref(a), None) == -1
