@@ -6,6 +6,9 @@ Workloads (the default is the one its metric is quoted on
         60-token batch prefill of N(0,1) embeddings, then greedy decode at B=1
         from token 151644.  A step is one decode token.          (default)
   cfg3  same model quantized W8A16, KV cache pre-filled to --context L.
+  cfg4  batch prefill of --rows (60 or 512) N(0,1) embeddings through the
+        28-layer FP16 model; a step is one prefill.  The four projections run on
+        the tcgen05 tensor cores; `roofline` is the gate|up GEMM timed alone.
   cfg5  batched W4A16 decode of 64 sequences with contexts U[128, 4096],
         sharded over ranks; a step advances every sequence by one token.
 
@@ -190,6 +193,16 @@ def cpu_decode_rate(mdir: str, quant: str, context: int, tokens: int, nthreads: 
     return tokens / (time.perf_counter() - t0)
 
 
+def cpu_prefill_rate(mdir: str, rows: int, nthreads: int):
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import ref_decoder as ref
+    dec = ref.RefDecoder(mdir, "fp16", max_seq_len=rows + 4, nthreads=nthreads)
+    emb = mf.seeded_hidden(830_000, rows, mf.ModelShape().hidden_dim)
+    t0 = time.perf_counter()
+    dec.prefill_batch(emb)
+    return rows / (time.perf_counter() - t0)
+
+
 # ─── arms ───
 
 def run_reference(args, world, rank):
@@ -197,12 +210,35 @@ def run_reference(args, world, rank):
         return None
     import torch  # noqa: F401  (only so the arm's environment matches the b200 arm)
     nth = os.cpu_count() or 1
-    quant = {"cfg2": "fp16", "cfg3": "int8", "cfg5": "int4"}[args.workload]
+    quant = {"cfg2": "fp16", "cfg3": "int8", "cfg4": "fp16", "cfg5": "int4"}[args.workload]
     mdir = model_dir(args.model_cache, quant, 0, 1)
     context = PREFILL if args.workload == "cfg2" else args.context
     tokens = args.warmup + args.steps
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import ref_decoder as ref
+    if args.workload == "cfg4":  # bounded sample: cpu_rows prefill rows per step
+        rows = max(1, args.cpu_rows)
+        emb = mf.seeded_hidden(830_000, rows, mf.ModelShape().hidden_dim)
+        d = ref.RefDecoder(mdir, quant, max_seq_len=rows + 4, nthreads=nth)
+        for _ in range(args.warmup):
+            d.seq_len = 0
+            d.prefill_batch(emb)
+        t = 0.0
+        for _ in range(args.steps):
+            d.seq_len = 0
+            t0 = time.perf_counter()
+            d.prefill_batch(emb)
+            t += time.perf_counter() - t0
+        rate = args.steps * rows / t
+        sample = f"{args.steps} prefills of {rows} rows of the 28-layer FP16 model, oracle C port, {nth} threads"
+        return {"metric": METRIC, "value": round(rate, 3), "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3 / args.steps, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded N(0,0.02) weights, N(0,1) embeddings)", "impl": "reference",
+                "config": {"workload": "cfg4", "model": "qwen3-0.6b-shaped", "rows": args.rows, "quant": quant},
+                "cpu_baseline": {"value": round(rate, 3), "unit": "tok/s", "cores": nth, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(rate, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     dec = ref.RefDecoder(mdir, quant, max_seq_len=context + tokens + 4, nthreads=nth)
     for layer in range(dec.nL):
         dec.set_kv(layer, 0, mf.seeded_kv(mf.kv_seed(layer, 0), context, dec.nkv, dec.hd),
@@ -318,6 +354,112 @@ def run_single_stream(args, world, rank, local):
     return line if rank == 0 else None
 
 
+def prefill_flops(shape: mf.ModelShape, rows: int) -> tuple[float, float]:
+    """(projection FLOPs, causal attention FLOPs) of one prefill of `rows` rows."""
+    proj = 2.0 * rows * sum(k * n for k, n in shape.proj_shapes().values()) * shape.num_layers
+    attn = 4.0 * shape.head_dim * shape.num_q_heads * shape.num_layers * rows * (rows + 1) / 2
+    return proj, attn
+
+
+def time_gemm_alone(rows: int, iters: int = 20):
+    """CUDA-event time of the gate|up b2_gemm launch (K=1024, 2x3072 rows) on
+    torch's current stream, L2 flushed (256 MB write) before every launch."""
+    import ctypes
+    import torch
+    import b200_decoder as bd
+    K, F = 1024, 3072
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x16 = torch.randn((rows, K), device="cuda", generator=g).half()
+    w = (torch.randn((2 * F, K), device="cuda", generator=g) * 0.02).half()
+    y = torch.empty((rows, F), device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    a = bd.B2GemmArgs(y.data_ptr(), F, x16.data_ptr(), K, rows, K, F, w.data_ptr(), None, bd.W_F16,
+                      bd.EPI_SILU_PAIR)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    times = []
+    for i in range(iters + 3):
+        flush.fill_(float(i))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        bd.check(bd.capi().b2_gemm(ctypes.byref(a), st), "b2_gemm")
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    ms = statistics.mean(times)
+    flops = 2.0 * rows * K * 2 * F
+    return ms, flops, w.numel() * 2 + x16.numel() * 2 + y.numel() * 4
+
+
+def run_prefill(args, world, rank, local):
+    import b200_decoder as bd
+    mdir = model_dir(args.model_cache, "fp16", rank, world)
+    bd.check(bd.capi().b2_set_device(local), "set_device")
+    import torch
+    torch.cuda.set_device(local)
+    shape = mf.ModelShape()
+    M, K, W = args.rows, args.steps, args.warmup
+    dec = bd.Decoder(mdir, "fp16", max_seq_len=M + 8)
+    emb = mf.seeded_hidden(830_000 + M, M, shape.hidden_dim)
+    for _ in range(W):
+        bd.capi().matmul_decoder_clear_kv_cache(dec.ctx)
+        dec.prefill_batch(emb)
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    dev_ms, host_s = [], []
+    t0 = time.perf_counter()
+    for _ in range(K):
+        bd.capi().matmul_decoder_clear_kv_cache(dec.ctx)
+        h0 = time.perf_counter()
+        dec.prefill_batch(emb)        # host embeddings -> device, all layers, synchronous
+        last = dec.hidden()           # device -> host read of the step's result
+        host_s.append(time.perf_counter() - h0)
+        dev_ms.append(dec.stats()["matmul_ms"])
+    t1 = time.perf_counter()
+    barrier(world)
+    clk = clocks.summary(t0, t1)
+    clocks.stop()
+    assert np.isfinite(last).all()
+    ms = max_over_ranks(world, statistics.mean(dev_ms))
+    e2e = max_over_ranks(world, statistics.mean(host_s))
+    g_ms, g_flops, g_bytes = time_gemm_alone(M)
+    g_ms = max_over_ranks(world, g_ms)
+    proj, attn = prefill_flops(shape, M)
+    peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    ach = g_flops / (g_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(world * M / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) embeddings)",
+        "config": {"workload": "cfg4", "model": "qwen3-0.6b-shaped (28 layers), FP16 layers", "rows": M,
+                   "parallelism": f"replicas x{world}",
+                   "l2": "weights 0.88 GB per prefill (> L2); gate|up GEMM timing flushes L2 (256 MB write) per launch"},
+        "prefill": {"tflops_projections": round(proj / (ms * 1e-3) / 1e12, 2),
+                    "tflops_with_attention": round((proj + attn) / (ms * 1e-3) / 1e12, 2),
+                    "projection_gflop": round(proj / 1e9, 2), "attention_gflop": round(attn / 1e9, 2)},
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(ach / peak, 4), "traffic": None,
+                     "kernel": f"b2_gemm gate|up + SiLU (M={M}, K=1024, N=2x3072), {round(g_ms * 1e3, 2)} us/launch",
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops (measured, burst)" if peaks else "fallback"},
+        "clocks": clk,
+        "e2e": {"value": round(world * M / e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": M * shape.hidden_dim * 4,
+                "d2h_bytes_per_step": shape.hidden_dim * 4, "api": "matmul_decoder_prefill_batch (C ABI)"},
+        "gpu_launches": K * shape.num_layers * 11,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        rows = max(1, args.cpu_rows)
+        rate = cpu_prefill_rate(mdir, rows, os.cpu_count() or 1)
+        line["cpu_baseline"] = {"value": round(rate, 4), "unit": "tok/s", "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": f"one {rows}-row prefill of the same 28-layer FP16 model, "
+                                                          f"oracle C port, all threads"}
+    dec.close()
+    return line if rank == 0 else None
+
+
 def run_batched(args, world, rank, local):
     import b200_decoder as bd
     mdir = model_dir(args.model_cache, "int4", rank, world)
@@ -362,7 +504,9 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg5"), default="cfg2")
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5"), default="cfg2")
+    ap.add_argument("--rows", type=int, default=512, help="cfg4 prefill rows (60 or 512)")
+    ap.add_argument("--cpu-rows", type=int, default=4, help="cfg4 CPU baseline sample rows")
     ap.add_argument("--context", type=int, default=128, help="cfg3 pre-filled context")
     ap.add_argument("--seqs", type=int, default=64, help="cfg5 total sequences")
     ap.add_argument("--model-cache", default=os.environ.get("B2_MODEL_CACHE", "/tmp/b2_bench_models"))
@@ -376,6 +520,8 @@ def main():
             line = run_reference(args, world, rank)
         elif args.workload == "cfg5":
             line = run_batched(args, world, rank, local)
+        elif args.workload == "cfg4":
+            line = run_prefill(args, world, rank, local)
         else:
             line = run_single_stream(args, world, rank, local)
         if line is not None:

@@ -654,6 +654,8 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
     b2_set_device(ctx->device);
     DevModel* m = &ctx->model;
     const int H = m->cfg.hidden_dim;
+    const double t0 = now_ms();
+    float dev_ms = 0.f;
     for (int off = 0; off < M; off += ctx->rows_cap) {
         const int rows = M - off < ctx->rows_cap ? M - off : ctx->rows_cap;
         for (int i = 0; i < rows; i++) ctx->h_pos[i] = ctx->seq_len + i;
@@ -664,13 +666,22 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
         if (split < 1) split = 1;
         if (split > ctx->split_decode) split = ctx->split_decode;
         LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, split, ctx->x16};
+        if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
         if (!rc) rc = md_enqueue_layers(m, &lb, rows, &kv, ctx->stream);
+        if (!rc) rc = b2_event_record(ctx->ev[1], ctx->stream);
         if (!rc) rc = b2_stream_sync(ctx->stream);
+        float ms = 0.f;
+        if (!rc) rc = b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[1]);
         if (rc) return fail("prefill_batch", rc);
+        dev_ms += ms;
         ctx->seq_len += rows;
         ctx->hidden_row = rows - 1;
         ctx->hidden_mk = 0;
     }
+    /* stats of the call: wall time, and the device time of the layer stack */
+    ctx->stats.total_ms = (float)(now_ms() - t0);
+    ctx->stats.matmul_ms = dev_ms;
+    ctx->stats.lm_head_ms = 0.f;
     return MATMUL_DECODER_OK;
 }
 
