@@ -116,7 +116,7 @@ int b2_rows_to_f16(uint16_t* y16, int ldy, const float* x, int ldx, int M, int K
  * the sum runs on the 5th-generation tensor cores (tcgen05.mma, FP16
  * operands staged by TMA, FP32 accumulator in tensor memory), so the
  * numerics equal b2_gemv's up to the FP32 summation order.  Shapes: K a
- * multiple of 64, N a multiple of 128 (of 64 for SILU_PAIR), ldx a multiple
+ * multiple of 64, N a multiple of 128, ldx a multiple
  * of 8; x16 and W 16-byte aligned.  Same role as b2_gemv in the reference
  * map (run_batch_matmul, src/matmul_decoder.c:1841-1899). */
 typedef struct {

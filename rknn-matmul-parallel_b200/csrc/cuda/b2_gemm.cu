@@ -8,7 +8,7 @@
 //
 //   warp 0       one thread issues TMA tile loads (cp.async.bulk.tensor, 128-byte
 //                swizzle) of a 128-row weight tile and a BN-row activation tile
-//                per 64-wide k step into a 4-stage shared-memory ring;
+//                per 64-wide k step into a 6-8 stage shared-memory ring;
 //   warp 1       allocates the tensor-memory accumulator (128 lanes x BN FP32
 //                columns) and one thread issues tcgen05.mma (M=128, N=BN, K=16,
 //                FP16 x FP16 -> FP32), committing each stage back to the loader;
@@ -17,9 +17,10 @@
 //
 // The weight tile is the MMA's A operand (output columns are TMEM lanes) and
 // the activation tile its B operand (token rows are TMEM columns), so one
-// CTA computes a 128-column x BN-row block of y.  For SILU_PAIR the A tile is
-// 64 gate rows followed by the 64 matching up rows; the up half crosses to
-// the gate half through shared memory in the epilogue.
+// CTA computes a 128-column x BN-row block of y.  For SILU_PAIR the stage
+// holds 128 gate rows and the 128 matching up rows; two MMAs per k step sum
+// them into TMEM columns [0, BN) and [BN, 2 BN), so each epilogue thread
+// finds the gate and up sums of its channel side by side.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is looked up at run time
 
 #include <mutex>
@@ -30,8 +31,18 @@ namespace {
 
 constexpr int kBM = 128;     // weight rows per tile (MMA M)
 constexpr int kBK = 64;      // k per stage: 64 FP16 = one 128-byte swizzle row
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
+// ring depth: as many 64-wide k stages as fit in ~192 KB (bytes in flight
+// hide the L2/DRAM latency of the tile loads)
+template <int BN, bool PAIR>
+__host__ __device__ constexpr int stage_bytes() {
+    return (PAIR ? 2 : 1) * kBM * 128 + BN * 128;
+}
+template <int BN, bool PAIR>
+__host__ __device__ constexpr int stages_for() {
+    return (192 * 1024) / stage_bytes<BN, PAIR>() > 8 ? 8 : (192 * 1024) / stage_bytes<BN, PAIR>();
+}
+constexpr int kMaxStages = 8;
 constexpr long long kWaitLimit = 1ll << 22;
 
 struct GemmParams {
@@ -43,8 +54,8 @@ struct GemmParams {
 };
 
 struct Bars {
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t done;
     uint32_t tmem;
     int failed;
@@ -133,11 +144,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    constexpr int kABytes = kBM * 128, kBBytes = BN * 128, kStage = kABytes + kBBytes;
+    constexpr int kABytes = (PAIR ? 2 : 1) * kBM * 128, kStage = stage_bytes<BN, PAIR>();
+    constexpr int kStages = stages_for<BN, PAIR>();
+    constexpr int kCols = PAIR ? 2 * BN : BN;  // TMEM columns (a power of two >= 32)
     Bars* b = reinterpret_cast<Bars*>(smem + kStages * kStage);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BN;
-    const int KT = g.K / kBK;
+    // split-K (ADD epilogue only): this CTA sums k stages [kt0, kt1)
+    const int KT_all = g.K / kBK;
+    const int kt0 = (int)((long long)KT_all * blockIdx.z / gridDim.z);
+    const int KT = (int)((long long)KT_all * (blockIdx.z + 1) / gridDim.z) - kt0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
@@ -152,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (warp == 1) {  // accumulator: 128 lanes x BN FP32 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&b->tmem)),
-                     "r"(BN)
+                     "r"(kCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -170,13 +186,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kt >= kStages && !mbar_wait(&b->empty[s], (uint32_t)((kt / kStages - 1) & 1), b)) break;
                 unsigned char* sa = smem + s * kStage;
                 mbar_expect_tx(&b->full[s], kStage);
+                const int kx = (kt0 + kt) * kBK;
                 if (PAIR) {
-                    tma_load_2d(sa, &tw, kt * kBK, 64 * blockIdx.x, &b->full[s]);
-                    tma_load_2d(sa + 64 * 128, &tw, kt * kBK, g.N + 64 * blockIdx.x, &b->full[s]);
+                    tma_load_2d(sa, &tw, kx, kBM * blockIdx.x, &b->full[s]);
+                    tma_load_2d(sa + kBM * 128, &tw, kx, g.N + kBM * blockIdx.x, &b->full[s]);
                 } else {
-                    tma_load_2d(sa, &tw, kt * kBK, kBM * blockIdx.x, &b->full[s]);
+                    tma_load_2d(sa, &tw, kx, kBM * blockIdx.x, &b->full[s]);
                 }
-                tma_load_2d(sa + kABytes, &tx, kt * kBK, m0, &b->full[s]);
+                tma_load_2d(sa + kABytes, &tx, kx, m0, &b->full[s]);
             }
         }
     } else if (warp == 1) {
@@ -188,8 +205,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + s * kStage), sb = sa + kABytes;
 #pragma unroll
-                for (int k = 0; k < kBK / 16; k++)  // K = 16 per MMA: 32 bytes along the swizzled row
+                for (int k = 0; k < kBK / 16; k++) {  // K = 16 per MMA: 32 bytes along the swizzled row
                     umma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (kt | k) != 0);
+                    if (PAIR)  // up rows into the next BN columns
+                        umma_f16(tmem + BN, sw128_desc(sa + kBM * 128 + 32 * k), sw128_desc(sb + 32 * k), idesc,
+                                 (kt | k) != 0);
+                }
                 umma_commit(&b->empty[s]);
             }
             umma_commit(&b->done);
@@ -201,45 +222,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!PAIR) {
             const int n = kBM * blockIdx.x + 32 * quad + lane;
             const float sc = g.scales ? g.scales[n] : 1.f;
+            const bool split = gridDim.z > 1;  // partial sums: add atomically into y
 #pragma unroll 1
             for (int c0 = 0; c0 < BN && ok; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
+                const int jn = min(16, g.M - (m0 + c0));
+                if (jn <= 0) break;
+                float* yp = g.y + (size_t)(m0 + c0) * g.ldy + n;
+                if (split) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int m = m0 + c0 + j;
-                    if (m >= g.M) break;
-                    float* yp = g.y + (size_t)m * g.ldy + n;
-                    const float val = __uint_as_float(v[j]) * sc;
-                    *yp = g.epilogue == B2_EPI_ADD ? *yp + val : val;
+                    for (int j = 0; j < 16; j++)
+                        if (j < jn) atomicAdd(yp + (size_t)j * g.ldy, __uint_as_float(v[j]) * sc);
+                } else if (g.epilogue == B2_EPI_ADD) {
+                    float old[16];  // all loads first, then the stores
+#pragma unroll
+                    for (int j = 0; j < 16; j++) old[j] = j < jn ? yp[(size_t)j * g.ldy] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < jn) yp[(size_t)j * g.ldy] = old[j] + __uint_as_float(v[j]) * sc;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < jn) yp[(size_t)j * g.ldy] = __uint_as_float(v[j]) * sc;
                 }
             }
         } else {
-            // lanes 0-63: gate rows of channels ch0..ch0+63, lanes 64-127: the up rows
-            float* xch = reinterpret_cast<float*>(smem);  // [64][17]; the stage ring is idle now
-            const int ch = 64 * blockIdx.x + 32 * (quad & 1) + lane;
-            const bool up = quad >= 2;
-            const float sc = g.scales ? g.scales[up ? g.N + ch : ch] : 1.f;
+            // lane = channel: gate sum in columns [0, BN), up sum in [BN, 2 BN)
+            const int ch = kBM * blockIdx.x + 32 * quad + lane;
+            const float sg = g.scales ? g.scales[ch] : 1.f, su = g.scales ? g.scales[g.N + ch] : 1.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                uint32_t v[16];
-                if (ok) tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
-                if (up)
+            for (int c0 = 0; c0 < BN && ok; c0 += 16) {
+                uint32_t vg[16], vu[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, vg);
+                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + BN + c0, vu);
+                const int jn = min(16, g.M - (m0 + c0));
+                if (jn <= 0) break;
+                float* yp = g.y + (size_t)(m0 + c0) * g.ldy + ch;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) xch[(32 * (quad & 1) + lane) * 17 + j] = __uint_as_float(v[j]) * sc;
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (!up && ok) {
-#pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int m = m0 + c0 + j;
-                        if (m >= g.M) break;
-                        const float gv = __uint_as_float(v[j]) * sc;
-                        const float uv = xch[(32 * quad + lane) * 17 + j];
-                        const float sig = 1.0f / (1.0f + expf(-gv));
-                        g.y[(size_t)m * g.ldy + ch] = (gv * sig) * uv;
-                    }
+                for (int j = 0; j < 16; j++) {
+                    if (j >= jn) break;
+                    const float gv = __uint_as_float(vg[j]) * sg, uv = __uint_as_float(vu[j]) * su;
+                    const float sig = 1.0f / (1.0f + expf(-gv));
+                    yp[(size_t)j * g.ldy] = (gv * sig) * uv;
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
             }
         }
     }
@@ -248,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
     }
 }
 
@@ -317,13 +343,12 @@ int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, u
 }
 
 template <int BN, bool PAIR>
-int launch(const B2GemmArgs* a, cudaStream_t s) {
+int launch(const B2GemmArgs* a, cudaStream_t s, int sms) {
     CUtensorMap tw, tx;
-    int rc = make_map(&tw, a->w, (uint64_t)a->K, (uint64_t)(PAIR ? 2 * a->N : a->N), (uint64_t)a->K * 2,
-                      PAIR ? 64 : kBM);
+    int rc = make_map(&tw, a->w, (uint64_t)a->K, (uint64_t)(PAIR ? 2 * a->N : a->N), (uint64_t)a->K * 2, kBM);
     if (!rc) rc = make_map(&tx, a->x16, (uint64_t)a->K, (uint64_t)a->M, (uint64_t)a->ldx * 2, BN);
     if (rc) return rc;
-    constexpr size_t smem = (size_t)kStages * (kBM * 128 + BN * 128) + sizeof(Bars) + 1024;
+    constexpr size_t smem = (size_t)stages_for<BN, PAIR>() * stage_bytes<BN, PAIR>() + sizeof(Bars) + 1024;
     auto fn = gemm_kernel<BN, PAIR>;
     static std::once_flag once[8];
     int dev = 0;
@@ -332,8 +357,13 @@ int launch(const B2GemmArgs* a, cudaStream_t s) {
     std::call_once(once[dev & 7], [&] { e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm smem attr: %s", cudaGetErrorString(e));
     GemmParams g{a->y, a->ldy, a->M, a->K, a->N, a->scales, a->epilogue};
-    const dim3 grid(PAIR ? a->N / 64 : a->N / kBM, (a->M + BN - 1) / BN);
-    e = b2::launch_pdl(fn, grid, dim3(kThreads), smem, s, tw, tx, g);
+    const int gx = a->N / kBM, gy = (a->M + BN - 1) / BN;
+    // A residual-add GEMM whose grid leaves SMs idle splits K over more CTAs
+    // (each adds its partial sum into y; at least 4 k stages per split).
+    int split = 1;
+    if (!PAIR && a->epilogue == B2_EPI_ADD)
+        while (gx * gy * split * 2 <= sms && (a->K / kBK) / (split * 2) >= 4) split *= 2;
+    e = b2::launch_pdl(fn, dim3(gx, gy, split), dim3(kThreads), smem, s, tw, tx, g);
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm launch: %s", cudaGetErrorString(e));
     return 0;
 }
@@ -345,15 +375,17 @@ extern "C" int b2_gemm(const B2GemmArgs* a, b2_stream_t stream) {
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_gemm: bad arguments");
     if (a->M == 0) return 0;
     const bool pair = a->epilogue == B2_EPI_SILU_PAIR;
-    if (a->wtype != B2_W_F16 || a->K % kBK || a->N % (pair ? 64 : kBM) || a->ldx % 8 || a->ldx < a->K ||
+    if (a->wtype != B2_W_F16 || a->K % kBK || a->N % kBM || a->ldx % 8 || a->ldx < a->K ||
         a->ldy < (pair ? a->N : a->N) || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
         (reinterpret_cast<uintptr_t>(a->w) & 15))
         return b2_set_error(B2_ERR_INVALID_ARG,
-                            "b2_gemm: needs FP16 weights, K %% 64 == 0, N %% %d == 0, ldx %% 8 == 0, aligned operands",
-                            pair ? 64 : kBM);
+                            "b2_gemm: needs FP16 weights, K %% 64 == 0, N %% 128 == 0, ldx %% 8 == 0, aligned operands");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (a->M <= 64) return pair ? launch<64, true>(a, s) : launch<64, false>(a, s);
-    return pair ? launch<128, true>(a, s) : launch<128, false>(a, s);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (a->M <= 64) return pair ? launch<64, true>(a, s, sms) : launch<64, false>(a, s, sms);
+    return pair ? launch<128, true>(a, s, sms) : launch<128, false>(a, s, sms);
 }
 
 extern "C" int b2_rows_to_f16(uint16_t* y16, int ldy, const float* x, int ldx, int M, int K, const float* norm_w,

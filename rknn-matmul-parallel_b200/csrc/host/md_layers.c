@@ -39,9 +39,8 @@ static int gemm_enabled(void) {
 /* One matmul of the layer: the GEMV, or for M >= MD_GEMM_MIN_ROWS rows of
  * FP16 weights the same operation on the tensor cores. */
 static int linear(const LayerBuffers* b, const B2GemvArgs* a, b2_stream_t s) {
-    const int pair = a->epilogue == B2_EPI_SILU_PAIR;
     if (b->x16 && a->M >= MD_GEMM_MIN_ROWS && a->wtype == B2_W_F16 && a->K % 64 == 0 &&
-        a->N % (pair ? 64 : 128) == 0 && gemm_enabled()) {
+        a->N % 128 == 0 && gemm_enabled()) {
         int rc = b2_rows_to_f16(b->x16, a->K, a->x, a->ldx, a->M, a->K, a->norm_w, a->eps, s);
         if (rc) return rc;
         B2GemmArgs g = {a->y, a->ldy, b->x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype, a->epilogue};
