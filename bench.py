@@ -325,7 +325,9 @@ def run_single_stream(args, world, rank, local):
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
         traffic = json.load(open(tp)).get(f"{args.workload}_bytes_per_token")
-    launches_per_token = 1 + shape.num_layers * 7 + 2 + 1
+    persistent = dec.uses_persistent_kernel()
+    # persistent kernel: one launch per token; graph: embed + 7 per layer + lm_head + argmax + loop advance
+    launches_per_token = 1 if persistent else 1 + shape.num_layers * 7 + 2 + 1
     line = {
         "metric": METRIC, "value": round(world * K / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": round(ms_tok, 4), "higher_is_better": True,
@@ -337,7 +339,9 @@ def run_single_stream(args, world, rank, local):
                    "l2": "inputs larger than L2: %.2f GB streamed per token" % (bpt / 1e9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "whole decode step (CUDA graph)", "bytes_per_token": int(bpt),
+                     "kernel": "whole decode step (" + ("persistent kernel b2_mk_decode, one launch" if persistent
+                                                        else "CUDA graph of per-op kernels") + ")",
+                     "bytes_per_token": int(bpt),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback"},
         "clocks": clk,
         "e2e": {"value": round(world * K / e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * (8 + shape.hidden_dim),

@@ -327,6 +327,12 @@ int matmul_decoder_set_seq_len(MatmulDecoderContext* ctx, int n);
  * prefill_batch), before the final norm, to host FP32 [hidden_dim]. */
 int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out);
 
+/* ADDITIVE.  1 when single-token steps run as the persistent decode kernel
+ * (one launch per token), 0 when they replay the graph of per-op kernels
+ * (B2_DECODE_KERNEL=graph at create time, or shapes the kernel does not
+ * cover). */
+int matmul_decoder_uses_persistent_kernel(const MatmulDecoderContext* ctx);
+
 /* ADDITIVE.  Quantize one FP16 [K][N] weight on the host into the on-disk
  * quantized layout: bits = 8 writes int8 [K][N]; bits = 4 writes int4 [K][N/2]
  * (low nibble = even column).  scales_out gets FP32 [N].  Bit-exact with the

@@ -12,12 +12,12 @@
  * serves every position.  Logits cross to the host only when the caller
  * passes a logits buffer.
  *
- * With B2_DECODE_KERNEL=persistent in the environment at create time, and
- * when the shapes allow it (INT8 lm_head, GQA group <= 2, head_dim 128), a
+ * When the shapes allow it (INT8 lm_head, GQA group <= 2, head_dim 128), a
  * single-token step runs instead as ONE launch of the persistent decode
  * kernel (b2_mk_decode), which streams the whole token's weights from one
- * CTA per SM.  The graph is the default while it is the faster of the two.
- * Batch prefill always uses the multi-kernel pass.
+ * CTA per SM; B2_DECODE_KERNEL=graph in the environment at create time keeps
+ * the graph of per-op kernels.  Batch prefill always uses the multi-kernel
+ * pass.
  */
 #include <stdio.h>
 #include <stdlib.h>
@@ -27,6 +27,13 @@
 #include "md_internal.h"
 
 #define PARAMS_INTS 8 /* [0] token, [1] use_embedding, [4] position */
+
+/* Context length up to which a single-token step uses the persistent kernel:
+ * beyond it the graph path's split-KV attention is faster (B200, W8A16:
+ * persistent 0.84 / 1.11 / 1.79 ms and graph 1.22 / 1.33 / 1.44 ms per token
+ * at 128 / 1024 / 4096 cached positions).  B2_MK_MAX_CONTEXT overrides it at
+ * create time. */
+#define MD_MK_MAX_CONTEXT 2048
 
 struct MatmulDecoderContext {
     DevModel model;
@@ -50,6 +57,7 @@ struct MatmulDecoderContext {
     int* h_loop;   /* pinned [4] */
     b2_graph_t g_head, g_nohead, g_loop;
     int use_mk;       /* persistent decode kernel selected */
+    int mk_max_ctx;   /* ... for steps below this many cached positions */
     int hidden_mk;    /* last token's hidden lives in the persistent kernel's scratch */
     B2MkPlan mk;
     B2MkLayer* d_mk_layers; /* device copy of the per-layer pointer table */
@@ -167,7 +175,7 @@ static void mk_setup(MatmulDecoderContext* ctx) {
     const char* env = getenv("B2_DECODE_KERNEL");
     DevModel* m = &ctx->model;
     const MatmulDecoderConfig* c = &m->cfg;
-    if (!env || strcmp(env, "persistent") != 0 || m->n_lm_heads > 1 || m->lm_wtype != B2_W_I8 ||
+    if ((env && strcmp(env, "graph") == 0) || m->n_lm_heads > 1 || m->lm_wtype != B2_W_I8 ||
         c->num_layers > B2_MK_MAX_LAYERS)
         return;
     B2MkPlan* p = &ctx->mk;
@@ -223,6 +231,8 @@ static void mk_setup(MatmulDecoderContext* ctx) {
     free(table);
     p->layers = ctx->d_mk_layers;
     ctx->use_mk = !rc && b2_mk_check(p) == 0;
+    const char* mx = getenv("B2_MK_MAX_CONTEXT");
+    ctx->mk_max_ctx = mx && atoi(mx) > 0 ? atoi(mx) : MD_MK_MAX_CONTEXT;
 }
 
 static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {
@@ -483,7 +493,7 @@ static int step_impl(MatmulDecoderContext* ctx, int token_id, const float* embed
     int rc = check_step_args(ctx, token_id, embedding, ctx ? ctx->model.cfg.vocab_size : 0);
     if (rc) return rc;
     b2_set_device(ctx->device);
-    if (ctx->use_mk) return mk_step(ctx, token_id, embedding, with_head, logits_out);
+    if (ctx->use_mk && ctx->seq_len < ctx->mk_max_ctx) return mk_step(ctx, token_id, embedding, with_head, logits_out);
     const double t0 = now_ms();
     b2_graph_t* g = with_head ? &ctx->g_head : &ctx->g_nohead;
     if (!*g && (rc = build_graph(ctx, with_head, g))) return fail("graph capture", rc);
@@ -590,7 +600,7 @@ int matmul_decoder_decode_greedy(MatmulDecoderContext* ctx, int first_token, int
     const double t0 = now_ms();
     b2_set_device(ctx->device);
     int rc = 0;
-    if (ctx->use_mk) {
+    if (ctx->use_mk && ctx->seq_len + n_tokens <= ctx->mk_max_ctx) {
         int* st = ctx->h_mk_state;
         st[B2_MK_TOKEN] = first_token;
         st[B2_MK_POS] = ctx->seq_len;
@@ -686,6 +696,8 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
 }
 
 /* ─── state queries ─── */
+
+int matmul_decoder_uses_persistent_kernel(const MatmulDecoderContext* ctx) { return ctx && ctx->use_mk ? 1 : 0; }
 
 void matmul_decoder_clear_kv_cache(MatmulDecoderContext* ctx) {
     if (ctx) ctx->seq_len = 0;

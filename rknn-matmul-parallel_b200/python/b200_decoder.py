@@ -89,6 +89,7 @@ SIGNATURES = {
     "matmul_decoder_get_kv": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_set_seq_len": (c_int, [c_vp, c_int]),
     "matmul_decoder_get_hidden": (c_int, [c_vp, c_vp]),
+    "matmul_decoder_uses_persistent_kernel": (c_int, [c_vp]),
     "matmul_decoder_quantize_weight": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_quantize_lm_head": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_batch_create": (c_vp, [ctypes.c_char_p, c_vp, c_int, c_int, c_int]),
@@ -253,6 +254,9 @@ class Decoder:
         h = np.empty(self.H, np.float32)
         check(capi().matmul_decoder_get_hidden(self.ctx, h.ctypes.data), "get_hidden")
         return h
+
+    def uses_persistent_kernel(self):
+        return bool(capi().matmul_decoder_uses_persistent_kernel(self.ctx))
 
     def stats(self):
         s = MatmulDecoderStats()

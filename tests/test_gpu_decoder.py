@@ -281,16 +281,28 @@ def test_pybind_module_on_gpu(small_models):
 
 # ── persistent decode kernel vs the multi-kernel graph path ──
 
-def graph_decoder(mdir, quant, **kw):
-    return bd.Decoder(mdir, quant, **kw)
-
-
-def persistent_decoder(mdir, quant, **kw):
-    os.environ["B2_DECODE_KERNEL"] = "persistent"
+def _decoder_with(kernel, mdir, quant, **kw):
+    old = os.environ.get("B2_DECODE_KERNEL")
+    os.environ["B2_DECODE_KERNEL"] = kernel
     try:
         return bd.Decoder(mdir, quant, **kw)
     finally:
-        del os.environ["B2_DECODE_KERNEL"]
+        if old is None:
+            del os.environ["B2_DECODE_KERNEL"]
+        else:
+            os.environ["B2_DECODE_KERNEL"] = old
+
+
+def graph_decoder(mdir, quant, **kw):
+    d = _decoder_with("graph", mdir, quant, **kw)
+    assert not d.uses_persistent_kernel()
+    return d
+
+
+def persistent_decoder(mdir, quant, **kw):
+    d = _decoder_with("persistent", mdir, quant, **kw)
+    assert d.uses_persistent_kernel()
+    return d
 
 
 @pytest.mark.parametrize("quant", ["fp16", "int8", "int4"])
@@ -321,8 +333,8 @@ def test_persistent_kernel_matches_graph_path(small_models, quant):
 
 def test_decode_greedy_graph_equals_step_loop(small_models):
     mdir = small_models["fp16"]
-    a = bd.Decoder(mdir, "fp16", max_seq_len=96)
-    b = bd.Decoder(mdir, "fp16", max_seq_len=96)
+    a = graph_decoder(mdir, "fp16", max_seq_len=96)
+    b = graph_decoder(mdir, "fp16", max_seq_len=96)
     toks, ms = a.decode_greedy(42, 12)
     ref_toks, t = [], 42
     for _ in range(12):
@@ -334,7 +346,7 @@ def test_decode_greedy_graph_equals_step_loop(small_models):
 def test_decode_greedy_equals_step_loop(small_models):
     mdir = small_models["int8"]
     a = persistent_decoder(mdir, "int8", max_seq_len=96)
-    b = bd.Decoder(mdir, "int8", max_seq_len=96)
+    b = graph_decoder(mdir, "int8", max_seq_len=96)
     emb = mf.seeded_hidden(872_000, 5, 1024)
     a.prefill_batch(emb)
     b.prefill_batch(emb)
@@ -350,7 +362,11 @@ def test_decode_greedy_equals_step_loop(small_models):
 def test_persistent_kernel_long_context(model_cache):
     """Attention split over many position ranges (L = 3000) plus the fresh position."""
     mdir = model(model_cache, "mk_long", "fp16", num_layers=2, vocab_size=4096, name="mk_long")
-    mk = persistent_decoder(mdir, "fp16", max_seq_len=3100)
+    os.environ["B2_MK_MAX_CONTEXT"] = "1000000"  # keep the persistent kernel past its default cut-over
+    try:
+        mk = persistent_decoder(mdir, "fp16", max_seq_len=3100)
+    finally:
+        del os.environ["B2_MK_MAX_CONTEXT"]
     gr = graph_decoder(mdir, "fp16", max_seq_len=3100)
     orc = ref.RefDecoder(mdir, "fp16", max_seq_len=3100, nthreads=NTH)
     for layer in range(2):
