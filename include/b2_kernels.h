@@ -49,6 +49,7 @@ enum {
     B2_EPI_STORE = 0,     /* y[m][n] = acc * s[n]                                   */
     B2_EPI_ADD = 1,       /* y[m][n] += acc * s[n]   (residual add)                 */
     B2_EPI_SILU_PAIR = 2, /* rows n and N+n: y[m][n] = silu(g) * u                  */
+    B2_EPI_ARGMAX = 3,    /* b2_gemm only: tokens[m] = argmax_n acc * s[n]           */
 };
 
 /* ─── runtime ─── */
@@ -110,14 +111,18 @@ int b2_gemv(const B2GemvArgs* a, b2_stream_t s);
 int b2_rows_to_f16(uint16_t* y16, int ldy, const float* x, int ldx, int M, int K, const float* norm_w,
                    float eps, b2_stream_t s);
 
-/* Tensor-core GEMM for M > 1 (batch prefill), FP16 weights:
- * y[m][n] = epi( s[n] * sum_k x16[m][k] * W[n][k] ) with the epilogues of
- * b2_gemv (SILU_PAIR: rows n and N+n).  x16 comes from b2_rows_to_f16;
- * the sum runs on the 5th-generation tensor cores (tcgen05.mma, FP16
- * operands staged by TMA, FP32 accumulator in tensor memory), so the
- * numerics equal b2_gemv's up to the FP32 summation order.  Shapes: K a
- * multiple of 64, N a multiple of 128, ldx a multiple
- * of 8; x16 and W 16-byte aligned.  Same role as b2_gemv in the reference
+/* Tensor-core GEMM for M > 1 (batch prefill, batched decode, batched
+ * lm_head): y[m][n] = epi( s[n] * sum_k x16[m][k] * W[n][k] ) with the
+ * epilogues of b2_gemv (SILU_PAIR: rows n and N+n) or ARGMAX (tokens[m] =
+ * the first n of the largest acc * s[n]; y, when not NULL, receives the
+ * logits).  x16 comes from b2_rows_to_f16; W is FP16, INT8 or INT4 in the
+ * device layout above (INT8/INT4 rows are widened exactly to FP16 on chip);
+ * the sum runs on the 5th-generation tensor cores (tcgen05.mma, operands
+ * staged by TMA, FP32 accumulator in tensor memory), so the numerics equal
+ * b2_gemv's up to the FP32 summation order.  Shapes: K a multiple of 64, N a
+ * multiple of 128 (any N for ARGMAX), ldx a multiple of 8; x16 and W 16-byte
+ * aligned.  ARGMAX needs keys: device scratch of b2_gemm_argmax_keys(M, N)
+ * bytes, and tokens: device int[M].  Same role as b2_gemv in the reference
  * map (run_batch_matmul, src/matmul_decoder.c:1841-1899). */
 typedef struct {
     float* y;
@@ -127,9 +132,12 @@ typedef struct {
     int M, K, N;
     const void* w;
     const float* scales;
-    int wtype; /* B2_W_F16 */
+    int wtype;
     int epilogue;
+    unsigned long long* keys;
+    int* tokens;
 } B2GemmArgs;
+size_t b2_gemm_argmax_keys(int M, int N);
 int b2_gemm(const B2GemmArgs* a, b2_stream_t s);
 
 /* Embedding: for row m, hidden[m] = use_staged && *use_staged ? staged[m]

@@ -48,8 +48,10 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(const float* __res
     // kernel, so reading them here is safe; lines the previous kernel is still
     // storing are harmless to prefetch because stores land in L2 and every
     // read below follows pdl_wait().
+    // Only the head of the range: with many sequences a whole-range prefetch
+    // would exceed L2 and evict itself before the loop gets there.
     if (threadIdx.x == 0 && p1 - 1 > p0) {
-        const uint32_t bytes = (uint32_t)(p1 - 1 - p0) * kHD * 2;
+        const uint32_t bytes = (uint32_t)min(p1 - 1 - p0, 4 * kGroups) * kHD * 2;
         b2::prefetch_l2(kv.k_base + head_off + (size_t)p0 * kHD, bytes);
         b2::prefetch_l2(kv.v_base + head_off + (size_t)p0 * kHD, bytes);
     }
@@ -75,49 +77,61 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(const float* __res
     const __half* vb = reinterpret_cast<const __half*>(kv.v_base + head_off) + sub * 16;
 
     // The loop bound is uniform across the warp (its four lane groups take
-    // positions pb .. pb+3) so every lane reaches the shuffles below; a group
-    // past the end of the range computes on zeros and keeps its state.
-    for (int pb = p0 + warp * 4; pb < p1; pb += kGroups) {
-        const int p = pb + (lane >> 3);
-        const bool live = p < p1;
-        uint4 k0 = make_uint4(0, 0, 0, 0), k1 = k0, v0 = k0, v1 = k0;
-        if (live) {
-            const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)p * kHD);
-            const uint4* vp = reinterpret_cast<const uint4*>(vb + (size_t)p * kHD);
-            k0 = kp[0];
-            k1 = kp[1];
-            v0 = vp[0];
-            v1 = vp[1];
-        }
-        float kf[16], vf[16];
-        const uint32_t* ku0 = &k0.x;
-        const uint32_t* ku1 = &k1.x;
-        const uint32_t* vu0 = &v0.x;
-        const uint32_t* vu1 = &v1.x;
+    // positions pb + {0,1,2,3} + 16 u) so every lane reaches the shuffles
+    // below; a group past the end of the range computes on zeros and keeps
+    // its state.  The K and V rows of kU positions per group are requested
+    // before any is used, so each lane keeps 4 x 64 bytes in flight.
+    constexpr int kU = 4;
+    for (int pb = p0 + warp * 4; pb < p1; pb += kGroups * kU) {
+        uint4 kr[kU][2], vr[kU][2];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float2 a = b2::h2_to_f2(ku0[i]), b = b2::h2_to_f2(ku1[i]);
-            kf[2 * i] = a.x; kf[2 * i + 1] = a.y; kf[8 + 2 * i] = b.x; kf[8 + 2 * i + 1] = b.y;
-            float2 c = b2::h2_to_f2(vu0[i]), d = b2::h2_to_f2(vu1[i]);
-            vf[2 * i] = c.x; vf[2 * i + 1] = c.y; vf[8 + 2 * i] = d.x; vf[8 + 2 * i + 1] = d.y;
+        for (int u = 0; u < kU; u++) {
+            const int p = pb + u * kGroups + (lane >> 3);
+            if (p < p1) {
+                const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)p * kHD);
+                const uint4* vp = reinterpret_cast<const uint4*>(vb + (size_t)p * kHD);
+                kr[u][0] = kp[0];
+                kr[u][1] = kp[1];
+                vr[u][0] = vp[0];
+                vr[u][1] = vp[1];
+            } else {
+                kr[u][0] = kr[u][1] = vr[u][0] = vr[u][1] = make_uint4(0, 0, 0, 0);
+            }
         }
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-            float d = 0.f;
+        for (int u = 0; u < kU; u++) {
+            if (pb + u * kGroups >= p1) break;  // uniform across the warp
+            const bool live = pb + u * kGroups + (lane >> 3) < p1;
+            float kf[16], vf[16];
+            const uint32_t* ku0 = &kr[u][0].x;
+            const uint32_t* ku1 = &kr[u][1].x;
+            const uint32_t* vu0 = &vr[u][0].x;
+            const uint32_t* vu1 = &vr[u][1].x;
 #pragma unroll
-            for (int j = 0; j < 16; j++) d = fmaf(qv[h][j], kf[j], d);
-            d += __shfl_xor_sync(0xffffffffu, d, 1);
-            d += __shfl_xor_sync(0xffffffffu, d, 2);
-            d += __shfl_xor_sync(0xffffffffu, d, 4);
-            if (!live) continue;
-            const float s = d * scale;
-            const float mn = fmaxf(mx[h], s);
-            const float corr = expf(mx[h] - mn);
-            const float pr = expf(s - mn);
-            ls[h] = ls[h] * corr + pr;
+            for (int i = 0; i < 4; i++) {
+                float2 a = b2::h2_to_f2(ku0[i]), b = b2::h2_to_f2(ku1[i]);
+                kf[2 * i] = a.x; kf[2 * i + 1] = a.y; kf[8 + 2 * i] = b.x; kf[8 + 2 * i + 1] = b.y;
+                float2 c = b2::h2_to_f2(vu0[i]), d = b2::h2_to_f2(vu1[i]);
+                vf[2 * i] = c.x; vf[2 * i + 1] = c.y; vf[8 + 2 * i] = d.x; vf[8 + 2 * i + 1] = d.y;
+            }
 #pragma unroll
-            for (int j = 0; j < 16; j++) o[h][j] = fmaf(pr, vf[j], o[h][j] * corr);
-            mx[h] = mn;
+            for (int h = 0; h < G; h++) {
+                float d = 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j++) d = fmaf(qv[h][j], kf[j], d);
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                d += __shfl_xor_sync(0xffffffffu, d, 4);
+                if (!live) continue;
+                const float sc = d * scale;
+                const float mn = fmaxf(mx[h], sc);
+                const float corr = expf(mx[h] - mn);
+                const float pr = expf(sc - mn);
+                ls[h] = ls[h] * corr + pr;
+#pragma unroll
+                for (int j = 0; j < 16; j++) o[h][j] = fmaf(pr, vf[j], o[h][j] * corr);
+                mx[h] = mn;
+            }
         }
     }
 #pragma unroll

@@ -11,7 +11,7 @@
  *   4. o_proj GEMV + residual add into hidden                       (b2_gemv ADD)
  *   5. RMSNorm(post_attn_norm) + gate|up GEMV + SiLU*mul            (b2_gemv SILU_PAIR)
  *   6. down GEMV + residual add into hidden                         (b2_gemv ADD)
- * With M >= MD_GEMM_MIN_ROWS rows and FP16 weights, steps 1, 4, 5 and 6 run
+ * With M >= MD_GEMM_MIN_ROWS rows, steps 1, 4, 5 and 6 run
  * as b2_rows_to_f16 (RMSNorm + FP16 rounding) + b2_gemm (tcgen05 tensor cores).
  * K/V of the current rows are stored before attention for decode and
  * prefill alike; the reference stores them after attention in prefill
@@ -36,14 +36,15 @@ static int gemm_enabled(void) {
     return v;
 }
 
-/* One matmul of the layer: the GEMV, or for M >= MD_GEMM_MIN_ROWS rows of
- * FP16 weights the same operation on the tensor cores. */
+/* One matmul of the layer: the GEMV, or for M >= MD_GEMM_MIN_ROWS rows the
+ * same operation on the tensor cores (FP16, INT8 or INT4 weights). */
 static int linear(const LayerBuffers* b, const B2GemvArgs* a, b2_stream_t s) {
-    if (b->x16 && a->M >= MD_GEMM_MIN_ROWS && a->wtype == B2_W_F16 && a->K % 64 == 0 &&
+    if (b->x16 && a->M >= MD_GEMM_MIN_ROWS && a->wtype != B2_W_F32 && a->K % 64 == 0 &&
         a->N % 128 == 0 && gemm_enabled()) {
         int rc = b2_rows_to_f16(b->x16, a->K, a->x, a->ldx, a->M, a->K, a->norm_w, a->eps, s);
         if (rc) return rc;
-        B2GemmArgs g = {a->y, a->ldy, b->x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype, a->epilogue};
+        B2GemmArgs g = {a->y, a->ldy, b->x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype, a->epilogue,
+                        NULL, NULL};
         return b2_gemm(&g, s);
     }
     return b2_gemv(a, s);

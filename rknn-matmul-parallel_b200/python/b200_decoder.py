@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(PKG_DIR, "lib", "libmatmul_decoder.so")
 c_int, c_float, c_vp, c_size = ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 QUANT = {"fp16": 0, "int8": 1, "int4": 2, "int4_g128": 3}
 W_F16, W_I8, W_I4, W_F32 = 0, 1, 2, 3
-EPI_STORE, EPI_ADD, EPI_SILU_PAIR = 0, 1, 2
+EPI_STORE, EPI_ADD, EPI_SILU_PAIR, EPI_ARGMAX = 0, 1, 2, 3
 
 
 class MatmulDecoderConfig(ctypes.Structure):
@@ -51,7 +51,7 @@ class B2GemvArgs(ctypes.Structure):
 class B2GemmArgs(ctypes.Structure):
     _fields_ = [("y", c_vp), ("ldy", c_int), ("x16", c_vp), ("ldx", c_int), ("M", c_int),
                 ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
-                ("epilogue", c_int)]
+                ("epilogue", c_int), ("keys", c_vp), ("tokens", c_vp)]
 
 
 class B2KVRef(ctypes.Structure):
@@ -127,6 +127,7 @@ SIGNATURES = {
     "b2_graph_destroy": (c_int, [c_vp]),
     "b2_gemv": (c_int, [c_vp, c_vp]),
     "b2_gemm": (c_int, [c_vp, c_vp]),
+    "b2_gemm_argmax_keys": (ctypes.c_size_t, [c_int, c_int]),
     "b2_rows_to_f16": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_int, c_vp, c_float, c_vp]),
     "b2_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "b2_qk_rope_kv": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_float,

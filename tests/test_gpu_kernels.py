@@ -232,12 +232,82 @@ def test_gemm_tensor_cores_silu_pair(M):
     assert_close(y_d.cpu().numpy(), exp)
 
 
+@pytest.mark.parametrize("wtype", [bd.W_I8, bd.W_I4])
+@pytest.mark.parametrize("M", [16, 64, 130])
+def test_gemm_tensor_cores_quantized_weights(wtype, M):
+    """INT8 / INT4 rows widened on chip to FP16 for tcgen05, against the C oracle."""
+    rng = np.random.default_rng(6100 + 10 * wtype + M)
+    for (K, N), epi in (((1024, 4096), bd.EPI_STORE), ((2048, 1024), bd.EPI_ADD)):
+        wf, s, rwt = make_weight(rng, K, N, wtype)
+        x = rng.standard_normal((M, K), dtype=np.float32)
+        y0 = rng.standard_normal((M, N), dtype=np.float32)
+        exp = ref.gemm(x, wf, s, wtype=rwt, n=N) + (y0 if epi == bd.EPI_ADD else 0)
+        x16 = rows_f16(dev(x), M, K)
+        y_d = dev(y0.copy())
+        a = bd.B2GemmArgs(y_d.data_ptr(), N, x16.data_ptr(), K, M, K, N, dev(device_rows(wf, wtype, N)).data_ptr(),
+                          dev(s).data_ptr(), wtype, epi, None, None)
+        bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm quantized")
+        torch.cuda.synchronize()
+        assert_close(y_d.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("wtype", [bd.W_I8, bd.W_I4])
+def test_gemm_tensor_cores_quantized_silu_pair(wtype):
+    K, F, M = 1024, 3072, 64
+    rng = np.random.default_rng(6200 + wtype)
+    wg, sg, rwt = make_weight(rng, K, F, wtype)
+    wu, su, _ = make_weight(rng, K, F, wtype)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    xn = np.stack([ref.rms_norm(r, norm_w) for r in x])
+    g, u = ref.gemm(xn, wg, sg, wtype=rwt, n=F), ref.gemm(xn, wu, su, wtype=rwt, n=F)
+    exp = np.stack([ref.silu_mul(g[i], u[i]) for i in range(M)])
+    rows = np.concatenate([device_rows(wg, wtype, F), device_rows(wu, wtype, F)])
+    x16 = rows_f16(dev(x), M, K, norm_w)
+    y_d = torch.zeros((M, F), dtype=torch.float32, device=DEV)
+    a = bd.B2GemmArgs(y_d.data_ptr(), F, x16.data_ptr(), K, M, K, F, dev(rows).data_ptr(),
+                      dev(np.concatenate([sg, su])).data_ptr(), wtype, bd.EPI_SILU_PAIR, None, None)
+    bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm quantized pair")
+    torch.cuda.synchronize()
+    assert_close(y_d.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("V", [8192, 151936, 70001])
+def test_gemm_tensor_cores_lm_head_argmax(V):
+    """Batched INT8 lm_head on the tensor cores: logits vs the oracle and
+    argmax of the kernel's own logits (first index on ties)."""
+    K, M = 1024, 64
+    rng = np.random.default_rng(6300 + V)
+    emb = (rng.standard_normal((V, K)) * 0.02).astype(np.float32)
+    table = np.empty((V, K), np.int8)
+    scales = np.empty(V, np.float32)
+    bd.check(bd.capi().matmul_decoder_quantize_lm_head(emb.ctypes.data, V, K, table.ctypes.data, scales.ctypes.data))
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    x16 = rows_f16(dev(x), M, K, norm_w)
+    logits_d = torch.empty((M, V), dtype=torch.float32, device=DEV)
+    tok_d = torch.empty(M, dtype=torch.int32, device=DEV)
+    keys = torch.empty(bd.capi().b2_gemm_argmax_keys(M, V), dtype=torch.uint8, device=DEV)
+    a = bd.B2GemmArgs(logits_d.data_ptr(), V, x16.data_ptr(), K, M, K, V, dev(table).data_ptr(),
+                      dev(scales).data_ptr(), bd.W_I8, bd.EPI_ARGMAX, keys.data_ptr(), tok_d.data_ptr())
+    bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), "b2_gemm argmax")
+    torch.cuda.synchronize()
+    logits, toks = logits_d.cpu().numpy(), tok_d.cpu().numpy()
+    for m in range(0, M, 9):
+        exp = lm_reference(x[m], norm_w, table, scales, bd.W_I8)
+        assert_close(logits[m], exp, rtol=1e-3, atol=1e-3)
+    for m in range(M):
+        assert toks[m] == int(np.argmax(logits[m]))
+
+
 def test_gemm_rejects_unsupported_shapes():
-    a = bd.B2GemmArgs(16, 128, 16, 100, 32, 100, 128, 16, None, bd.W_F16, 0)   # K % 64
+    a = bd.B2GemmArgs(16, 128, 16, 100, 32, 100, 128, 16, None, bd.W_F16, 0, None, None)  # K % 64
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
-    a = bd.B2GemmArgs(16, 128, 16, 128, 32, 128, 128, 16, None, bd.W_I8, 0)    # quantized weights
+    a = bd.B2GemmArgs(16, 128, 16, 128, 32, 128, 128, 16, None, bd.W_I8, 0, None, None)  # INT8 without scales
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
-    a = bd.B2GemmArgs(16, 96, 16, 128, 32, 128, 96, 16, None, bd.W_F16, 0)     # N % 128
+    a = bd.B2GemmArgs(16, 96, 16, 128, 32, 128, 96, 16, None, bd.W_F16, 0, None, None)   # N % 128
+    assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
+    a = bd.B2GemmArgs(None, 0, 16, 128, 32, 128, 1000, 16, None, bd.W_F16, bd.EPI_ARGMAX, None, None)  # no keys
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
 
 
