@@ -464,6 +464,19 @@ def run_prefill(args, world, rank, local):
     return line if rank == 0 else None
 
 
+def shard_sequences(lens, world):
+    """Greedy bin-packing of sequences on context length (KV bytes dominate a
+    batched step): longest first, each to the rank with the least work so far.
+    Every rank computes the same assignment."""
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for s in sorted(range(len(lens)), key=lambda i: (-int(lens[i]), i)):
+        r = min(range(world), key=lambda i: (load[i], i))
+        parts[r].append(s)
+        load[r] += int(lens[s])
+    return [sorted(p) for p in parts]
+
+
 def run_batched(args, world, rank, local):
     import b200_decoder as bd
     mdir = model_dir(args.model_cache, "int4", rank, world)
@@ -471,7 +484,7 @@ def run_batched(args, world, rank, local):
     shape = mf.ModelShape()
     n_total = args.seqs
     lens = np.random.default_rng(55).integers(128, 4097, size=n_total)
-    mine = list(range(rank, n_total, world))
+    mine = shard_sequences(lens, world)[rank]
     K, W = args.steps, args.warmup
     bat = bd.BatchDecoder(mdir, len(mine), "int4", max_seq_len=4096 + K + W + 8)
 
