@@ -254,6 +254,10 @@ typedef struct {
     const float* post_norm;
     const float* q_norm;   /* NULL when the model has no q/k norm           */
     const float* k_norm;
+    const void* dn_t;      /* down_proj by input channel: [ffn][hidden]
+                              (FP16 / int8, or int4 [ffn][hidden/2] with
+                              the even output column in the low nibble);
+                              scales are dn_s                               */
 } B2MkLayer;
 
 typedef struct {

@@ -52,7 +52,8 @@ constexpr int kResCap = 64;        // per-item residual rows prefetched into sha
 constexpr long long kPollLimit = 1ll << 22;
 constexpr long long kBarLimit = 1ll << 22;
 
-enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM };
+enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM, IT_DNT };
+constexpr int kActCap = 64;   // gate|up channels per CTA (the down partial's inputs)
 
 // Vectors passed between CTAs are "LL" words (the low-latency protocol of
 // NCCL's LL transport): one 64-bit store holds an FP32 value in the low half
@@ -60,7 +61,8 @@ enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM };
 // it needs until every tag is this step's, so producers need no fence and no
 // flag, and a consumer starts as soon as its own inputs have landed.
 struct Scratch {
-    unsigned long long* cnt;   // [8]: [0] CTAs finished, [1] best argmax key
+    unsigned long long* cnt;   // [8 + L]: [0] CTAs finished, [1] best argmax key, [8 + l] down partials of layer l
+    float* hacc;               // [L][2][H] layer outputs, summed from down partials (two token parities)
     unsigned long long* hbuf;  // LL [L+1][H] layer inputs (row 0 unused: layer 0 reads the embedding)
     unsigned long long* hmid;  // LL [L][H] hidden after attention + residual
     unsigned long long* qkv;   // LL [L][qd + 2 kvd]
@@ -82,7 +84,8 @@ __host__ __device__ inline Scratch scratch_layout(void* base, int L, int H, int 
         off += align256(bytes);
         return r;
     };
-    s.cnt = reinterpret_cast<unsigned long long*>(take(8 * 8));
+    s.cnt = reinterpret_cast<unsigned long long*>(take((size_t)(8 + L) * 8));
+    s.hacc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
     s.hbuf = reinterpret_cast<unsigned long long*>(take((size_t)(L + 1) * H * 8));
     s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)L * H * 8));
     s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)L * (qd + 2 * kvd) * 8));
@@ -136,6 +139,20 @@ __device__ __forceinline__ unsigned long long atom_add_acqrel(unsigned long long
     unsigned long long old;
     asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
     return old;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Four FP32 additions into global memory in one request.
+__device__ __forceinline__ void red_add_v4(float* p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -305,7 +322,9 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
     const size_t rb_h = row_bytes(WT, H), rb_q = row_bytes(WT, geo.qd), rb_f = row_bytes(WT, F);
     // rows per stage, at most 64 (four 16-row tensor-core tiles)
     const int cap_h = min(64, kStageBytes / (int)rb_h), cap_q = min(64, kStageBytes / (int)rb_q);
-    const int cap_f = min(64, kStageBytes / (int)rb_f), cap_pair = min(32, kStageBytes / (2 * (int)rb_h));
+    const int cap_pair = min(32, kStageBytes / (2 * (int)rb_h));
+    const int cap_t = min(64, kStageBytes / (int)rb_h);  // input-major down rows: H values each
+    (void)rb_f;
     for (int l = 0; l < p.n_layers; l++) {
         const B2MkLayer& Lw = p.layers[l];
         if (v.stop()) return;
@@ -350,7 +369,7 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
             v.end(it);
         }
         if (v.stop()) return;
-        {  // gate|up channel pairs
+        {  // gate|up channel pairs, then the same channels' rows of the input-major down weight
             Item it{IT_GU, l, split_lo(F, geo.G, geo.cta), split_lo(F, geo.G, geo.cta + 1), 0, 0, 0, 0};
             v.begin(it);
             for (int a = it.r0; a < it.r1 && !v.stop(); a += cap_pair) {
@@ -360,16 +379,10 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
                         (const unsigned char*)Lw.gu + (size_t)(F + a) * rb_h, bytes, bytes};
                 v.chunk(c);
             }
-            v.end(it);
-        }
-        if (v.stop()) return;
-        {  // down rows
-            Item it{IT_DN, l, split_lo(H, geo.G, geo.cta), split_lo(H, geo.G, geo.cta + 1), 0, 0, 0, 0};
-            v.begin(it);
-            for (int a = it.r0; a < it.r1 && !v.stop(); a += cap_f) {
-                const int b = min(it.r1, a + cap_f);
-                Chunk c{IT_DN, l, a, b, 0, 0, (const unsigned char*)Lw.dn + a * rb_f, (uint32_t)((b - a) * rb_f),
-                        nullptr, 0, 0};
+            for (int a = it.r0; a < it.r1 && !v.stop(); a += cap_t) {
+                const int b = min(it.r1, a + cap_t);
+                Chunk c{IT_DNT, l, a, b, 0, 0, (const unsigned char*)Lw.dn_t + (size_t)a * rb_h,
+                        (uint32_t)((b - a) * rb_h), nullptr, 0, 0};
                 v.chunk(c);
             }
             v.end(it);
@@ -403,6 +416,7 @@ struct Shared {
     float gm[kCWarps][kMaxGq], gl[kCWarps][kMaxGq];  // per-warp softmax state
     float go[kCWarps][kMaxGq][kHD];                   // per-warp partial outputs
     float pr[kCWarps][16];      // per-warp partial row sums of a chunk
+    float act[kActCap];         // FP16-rounded SiLU(gate) * up of this CTA's channels
     float sc[2][kScCap];        // prefetched scales of the current / next item
     float res[2][kResCap];      // prefetched residual rows of the current / next item
 };
@@ -469,6 +483,8 @@ struct Consumer {
     int items = 0;   // items begun; its parity selects the prefetch buffers
     int buf = 0, r0 = 0, nrows = 0;  // current item: prefetch buffer, first row, row count
     const float* isc = nullptr;       // current item's scale array (null: FP16 weights)
+    float dacc_[4];                   // down partial of outputs 4 tid .. 4 tid + 3 (gate|up item)
+    float4 res4_;                     // CTA 0: hmid at those outputs (the residual it adds)
     // attention state of this thread's lane group (positions of group grp)
     float m_[kMaxGq], l_[kMaxGq], o_[kMaxGq][16], qv_[kMaxGq][16];
     unsigned long long best = 0ull;
@@ -547,6 +563,39 @@ struct Consumer {
             __nanosleep(128);
         }
         return true;
+    }
+
+    // Consumer 0 waits until *cnt >= want (bounded); the decision reaches every
+    // consumer through the barrier, and the barrier orders their reads of the
+    // data the counter publishes after consumer 0's acquire.
+    __device__ void wait_counter(const unsigned long long* cnt, unsigned long long want) {
+        if (tid == 0) {
+            for (long long it = 0; ld_acquire(cnt) < want; it++) {
+                if ((it & 63) == 63 && abort_seen()) {
+                    sh.cabort = 1;
+                    break;
+                }
+                if (it > kPollLimit) {
+                    sh.cabort = 1;
+                    atomicOr(p.state + B2_MK_ERR, 1);
+                    break;
+                }
+                if (it > 32) __nanosleep(64);
+            }
+        }
+        consumer_sync();
+        aborted = *(volatile int*)&sh.cabort != 0;
+    }
+    __device__ unsigned long long* dn_count(int l) const { return S.cnt + 8 + l; }
+    // output of layer l (input of layer l + 1) for this step's parity
+    __device__ float* layer_out(int l) const { return S.hacc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
+    // groups of a vector summed by other CTAs in this launch: read through L2
+    __device__ void cg_gather(const float* src, int K, float4 (&v)[kV]) const {
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int q = tid + j * kConsumers;
+            if (q * 4 < K) v[j] = __ldcg(reinterpret_cast<const float4*>(src) + q);
+        }
     }
 
     // Same groups of a plain FP32 vector that is constant during the launch.
@@ -645,7 +694,7 @@ struct Consumer {
         for (int i = tid; i < nrows; i += kConsumers) {
             float v = 0.f;
             if (ll) ok = ll_wait(ll + r0 + i, v) && ok;
-            else v = __ldg(plain + r0 + i);
+            else v = __ldcg(plain + r0 + i);
             sh.res[buf][i] = v;
         }
         return ok;
@@ -653,7 +702,7 @@ struct Consumer {
     __device__ float resid(const unsigned long long* ll, const float* plain, int i) const {
         if (nrows <= kResCap) return sh.res[buf][i];
         float v = 0.f;
-        if (!ll) return __ldg(plain + r0 + i);
+        if (!ll) return __ldcg(plain + r0 + i);
         ll_wait(ll + r0 + i, v);  // validated by this CTA's previous stage
         return v;
     }
@@ -720,8 +769,13 @@ struct Consumer {
                 isc = Lw.qkv_s;
                 load_scales(Lw.qkv_s, 0);
                 load_norm(Lw.in_norm, H);
-                if (it.l == 0) plain_gather(emb_row, H, v);
-                else ok = ll_gather(S.hbuf + (size_t)it.l * H, H, v);
+                if (it.l == 0) {
+                    plain_gather(emb_row, H, v);
+                } else {
+                    wait_counter(dn_count(it.l - 1), (unsigned long long)geo.G * tag);
+                    if (stop()) return;
+                    cg_gather(layer_out(it.l - 1), H, v);
+                }
                 settle(ok);
                 if (!stop()) stage(v, H, Lw.in_norm, perm);
                 break;
@@ -729,7 +783,7 @@ struct Consumer {
             case IT_O:
                 isc = Lw.o_s;
                 load_scales(Lw.o_s, 0);
-                ok = load_res(it.l == 0 ? nullptr : S.hbuf + (size_t)it.l * H, emb_row);
+                ok = load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1));
                 ok = attn_gather(it.l, v) && ok;
                 settle(ok);
                 if (!stop()) stage(v, geo.qd, nullptr, perm);
@@ -739,22 +793,20 @@ struct Consumer {
                 load_scales(Lw.gu_s, p.ffn);
                 load_norm(Lw.post_norm, H);
                 ok = ll_gather(S.hmid + (size_t)it.l * H, H, v);
+#pragma unroll
+                for (int i = 0; i < 4; i++) dacc_[i] = 0.f;
+                res4_ = v[0];  // CTA 0 adds hmid (outputs 4 tid ..) into the layer output
                 settle(ok);
                 if (!stop()) stage(v, H, Lw.post_norm, perm);
-                break;
-            case IT_DN:
-                isc = Lw.dn_s;
-                load_scales(Lw.dn_s, 0);
-                ok = load_res(S.hmid + (size_t)it.l * H, nullptr);
-                ok = ll_gather(S.act + (size_t)it.l * p.ffn, p.ffn, v) && ok;
-                settle(ok);
-                if (!stop()) stage(v, p.ffn, nullptr, perm);
                 break;
             case IT_LM:
                 isc = p.lm_s;
                 load_scales(p.lm_s, 0);
                 load_norm(p.final_norm, H);
-                ok = ll_gather(S.hbuf + (size_t)p.n_layers * H, H, v);
+                wait_counter(dn_count(p.n_layers - 1), (unsigned long long)geo.G * tag);
+                if (stop()) return;
+                cg_gather(layer_out(p.n_layers - 1), H, v);
+                if (geo.cta == 0) write_final(v);
                 settle(ok);
                 if (!stop()) stage(v, H, p.final_norm, false);  // int8 table
                 best = 0ull;
@@ -791,7 +843,7 @@ struct Consumer {
             case IT_ATTN: attn_chunk(c, buf_); break;
             case IT_O: rows_resid(c, buf_, geo.qd); break;
             case IT_GU: rows_gu(c, buf_); break;
-            case IT_DN: rows_resid(c, buf_, p.ffn); break;
+            case IT_DNT: rows_dnt(c, buf_); break;
             case IT_LM: rows_lm(c, buf_); break;
         }
         __syncwarp();  // this warp is done reading the stage
@@ -806,6 +858,23 @@ struct Consumer {
         if (stop()) return;
         if (it.type == IT_ATTN) {
             attn_epilogue(it);
+        } else if (it.type == IT_GU) {
+            // this CTA's down partial (its gate|up channels) into the layer
+            // output; CTA 0 also adds the residual hmid.  The barrier orders
+            // every consumer's additions before consumer 0's release.
+            const int n = 4 * tid;
+            if (n < p.hidden) {
+                const float* ds = p.layers[it.l].dn_s;
+                float4 d = make_float4(dacc_[0], dacc_[1], dacc_[2], dacc_[3]);
+                if (ds) {
+                    const float4 sc = __ldg(reinterpret_cast<const float4*>(ds + n));
+                    d.x *= sc.x, d.y *= sc.y, d.z *= sc.z, d.w *= sc.w;
+                }
+                if (geo.cta == 0) d.x += res4_.x, d.y += res4_.y, d.z += res4_.z, d.w += res4_.w;
+                red_add_v4(layer_out(it.l) + n, d);
+            }
+            consumer_sync();
+            if (tid == 0) red_release(dn_count(it.l), 1ull);
         } else if (it.type == IT_LM) {
             unsigned long long b = best;
 #pragma unroll
@@ -867,16 +936,11 @@ struct Consumer {
     __device__ void rows_resid(const Chunk& c, const unsigned char* buf_, int K) {
         const size_t rb = row_bytes(WT, K);
         const int H = p.hidden, n = c.b - c.a;
-        const bool is_o = c.type == IT_O;
         const float v = chunk_dot<WT>(n, K, [&](int r) { return buf_ + (size_t)r * rb; });
         if (tid < n) {
             const int r = c.a + tid;
-            const unsigned long long* res_ll =
-                is_o ? (c.l == 0 ? nullptr : S.hbuf + (size_t)c.l * H) : S.hmid + (size_t)c.l * H;
-            unsigned long long* dst = is_o ? S.hmid + (size_t)c.l * H : S.hbuf + (size_t)(c.l + 1) * H;
-            const float y = resid(res_ll, emb_row, r - r0) + v * scale(isc, r - r0, 0);
-            ll_put(dst + r, y, tag);
-            if (!is_o && c.l == p.n_layers - 1) S.hfinal[r] = y;
+            const float y = resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0) + v * scale(isc, r - r0, 0);
+            ll_put(S.hmid + (size_t)c.l * H + r, y, tag);
         }
     }
 
@@ -893,7 +957,45 @@ struct Consumer {
             const float g = v * scale(isc, j - r0, p.ffn);
             const float up = u * scale(isc, nrows + (j - r0), p.ffn);
             const float sig = 1.0f / (1.0f + expf(-g));
-            ll_put(S.act + (size_t)c.l * p.ffn + j, (g * sig) * up, tag);
+            sh.act[j - r0] = __half2float(__float2half_rn((g * sig) * up));  // the down matmul's FP16 input
+        }
+    }
+
+    // Down partial: outputs 4 tid .. 4 tid + 3 of rows j in [c.a, c.b) of the
+    // input-major down weight times the staged act[j] (exact FP16 x weight
+    // products, FP32 sums; the per-output scale is applied at the end).
+    __device__ void rows_dnt(const Chunk& c, const unsigned char* buf_) {
+        const int n = 4 * tid;
+        if (n >= p.hidden) return;
+        const size_t rb = row_bytes(WT, p.hidden);
+        for (int j = c.a; j < c.b; j++) {
+            const float a = sh.act[j - r0];
+            const unsigned char* row = buf_ + (size_t)(j - c.a) * rb;
+            float w[4];
+            if constexpr (WT == B2_W_F16) {
+                const uint2 h = *reinterpret_cast<const uint2*>(row + n * 2);
+                const float2 w01 = b2::h2_to_f2(h.x), w23 = b2::h2_to_f2(h.y);
+                w[0] = w01.x, w[1] = w01.y, w[2] = w23.x, w[3] = w23.y;
+            } else if constexpr (WT == B2_W_I8) {
+                const uint32_t u = b2::i8x4_bias(*reinterpret_cast<const uint32_t*>(row + n));
+                w[0] = b2::i8_from_biased<0>(u), w[1] = b2::i8_from_biased<1>(u);
+                w[2] = b2::i8_from_biased<2>(u), w[3] = b2::i8_from_biased<3>(u);
+            } else {
+                const uint32_t u = b2::i4x8_bias(*reinterpret_cast<const uint16_t*>(row + n / 2));
+                w[0] = b2::i4_from_biased<0>(u), w[1] = b2::i4_from_biased<1>(u);
+                w[2] = b2::i4_from_biased<2>(u), w[3] = b2::i4_from_biased<3>(u);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) dacc_[i] = fmaf(a, w[i], dacc_[i]);
+        }
+    }
+
+    // CTA 0: the final residual stream (before the final norm) for the host.
+    __device__ void write_final(const float4 (&v)[kV]) const {
+#pragma unroll
+        for (int j = 0; j < kV; j++) {
+            const int q = tid + j * kConsumers;
+            if (q * 4 < p.hidden) reinterpret_cast<float4*>(S.hfinal)[q] = v[j];
         }
     }
 
@@ -1184,7 +1286,25 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
         const int tok = p.state[B2_MK_TOKEN];
         const float* emb_row = p.state[B2_MK_USE_EMB] ? p.staged_emb : p.emb + (size_t)tok * p.hidden;
         Consumer<WT> cons{p, geo, sh, ring, xs, S, (uint32_t)(gen + 1), emb_row, tid, lane, warp};
+        {  // zero this CTA's slice of the next step's layer-output accumulators
+           // (the other parity; nothing reads it during this step)
+            float4* z = reinterpret_cast<float4*>(S.hacc);
+            const int per = p.hidden / 4;  // float4 per layer output
+            const int total = p.n_layers * per;
+            const int a = split_lo(total, geo.G, geo.cta), b = split_lo(total, geo.G, geo.cta + 1);
+            const unsigned npar = (unsigned)(gen + 2) & 1u;
+            for (int i = a + tid; i < b; i += kConsumers)
+                z[((size_t)(i / per) * 2 + npar) * per + (i % per)] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         walk<WT>(p, geo, cons);
+        if (!p.do_lm && geo.cta == 0 && !cons.stop()) {  // prefill-mode step: publish the final hidden
+            cons.wait_counter(cons.dn_count(p.n_layers - 1), (unsigned long long)geo.G * (gen + 1));
+            if (!cons.stop()) {
+                float4 v[kV];
+                cons.cg_gather(cons.layer_out(p.n_layers - 1), p.hidden, v);
+                cons.write_final(v);
+            }
+        }
         if (!cons.stop()) {  // FIN: the last CTA publishes the step
             consumer_sync();
             if (tid == 0) {
@@ -1244,6 +1364,8 @@ int launch(const B2MkPlan* p, cudaStream_t s) {
     }
     int sms = 0;
     B2_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if ((p->ffn + sms - 1) / sms > kActCap)  // gate|up channels of one CTA feed its down partial
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_mk_decode: ffn %d needs more than %d SMs", p->ffn, p->ffn / kActCap);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kThreads);
@@ -1283,7 +1405,7 @@ extern "C" int b2_mk_check(const B2MkPlan* p) {
     // lm_head included), and short enough to stage
     const int E = p->wtype == B2_W_F16 ? 32 : p->wtype == B2_W_I8 ? 64 : 128;
     if (p->hidden % E || p->ffn % E || (p->nq * kHD) % E || p->hidden % 64 || p->hidden > kMaxK ||
-        p->ffn > kMaxK || p->nq * kHD > kMaxK)
+        p->ffn > kMaxK || p->nq * kHD > kMaxK || p->hidden > 4 * kConsumers)
         return B2_ERR_INVALID_ARG;
     // every streamed row range must fit one stage at least one row at a time
     if (2 * row_bytes(p->wtype, p->hidden) > (size_t)kStageBytes || row_bytes(p->wtype, p->ffn) > (size_t)kStageBytes ||

@@ -220,6 +220,7 @@ static void mk_setup(MatmulDecoderContext* ctx) {
         d->gu_s = L->gu.s;
         d->dn = L->down.w;
         d->dn_s = L->down.s;
+        d->dn_t = L->down_t;
         d->in_norm = L->in_norm;
         d->post_norm = L->post_norm;
         const int qk = c->has_qk_norm && L->q_norm && L->k_norm;

@@ -30,6 +30,7 @@ typedef struct {
     DevProj o;     /* rows: hidden, K = nq*hd */
     DevProj gu;    /* rows: gate (ffn) | up (ffn) */
     DevProj down;  /* rows: hidden, K = ffn */
+    void* down_t;  /* down_proj in its file layout [ffn][hidden] (input-channel rows), same encoding */
     float *in_norm, *post_norm, *q_norm, *k_norm;
 } DevLayer;
 

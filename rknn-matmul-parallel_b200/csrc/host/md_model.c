@@ -68,7 +68,7 @@ size_t md_model_bytes(const MatmulDecoderConfig* c, int wtype, int max_seq, int 
         t += ALIGN_UP(V * H) + ALIGN_UP(V * 4);
     }
     size_t per_layer = proj_bytes(wtype, qd + 2 * kvd, (int)H) + proj_bytes(wtype, (int)H, qd) +
-                       proj_bytes(wtype, (int)(2 * F), (int)H) + proj_bytes(wtype, (int)H, (int)F) +
+                       proj_bytes(wtype, (int)(2 * F), (int)H) + 2 * proj_bytes(wtype, (int)H, (int)F) +
                        2 * ALIGN_UP(H * 4) + 2 * ALIGN_UP((size_t)c->head_dim * 4);
     t += per_layer * (size_t)c->num_layers;
     t += 2 * ALIGN_UP((size_t)max_seq * (c->head_dim / 2) * 4);
@@ -273,6 +273,41 @@ static int upload_proj(DevModel* m, DevProj* P, int rows, int K, const int* part
     return rc;
 }
 
+/* Projection i in its file layout ([K][N], int4 [K][N/2]) in the model's
+ * encoding, quantized at load like stage_rows when only FP16 exists.  The
+ * persistent decode kernel streams down_proj this way: one row per input
+ * channel with the output columns contiguous. */
+static int upload_file_layout(DevModel* m, void** dst, int proj, const HostLayer* L) {
+    int K, N;
+    proj_shape(&m->cfg, proj, &K, &N);
+    const int target = m->wtype, wt = L->wt[proj];
+    const void* use = L->w[proj];
+    uint8_t* tmpq = NULL;
+    float* tmps = NULL;
+    if (wt != target) {
+        if (wt != B2_W_F16) return MATMUL_DECODER_ERR_UNSUPPORTED;
+        const int bits = target == B2_W_I8 ? 8 : 4;
+        tmpq = (uint8_t*)malloc(bits == 8 ? (size_t)K * N : (size_t)K * N / 2);
+        tmps = (float*)malloc((size_t)N * 4);
+        if (!tmpq || !tmps) {
+            free(tmpq);
+            free(tmps);
+            return MATMUL_DECODER_ERR_MEMORY;
+        }
+        md_quantize_cols((const uint16_t*)use, K, N, bits, tmpq, tmps);
+        use = tmpq;
+    }
+    const size_t bytes = target == B2_W_F16 ? (size_t)K * N * 2 : target == B2_W_I8 ? (size_t)K * N : (size_t)K * N / 2;
+    int rc = 0;
+    *dst = md_arena_alloc(&m->arena, bytes);
+    if (!*dst) rc = MATMUL_DECODER_ERR_MEMORY;
+    if (!rc) rc = b2_memcpy_h2d(*dst, use, bytes, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    free(tmpq);
+    free(tmps);
+    return rc;
+}
+
 static float* upload_f32(DevModel* m, const float* src, size_t n) {
     float* d = (float*)md_arena_alloc(&m->arena, n * 4);
     if (!d) return NULL;
@@ -358,6 +393,7 @@ static int upload_common(DevModel* m, const float* emb, const float* lm_head, fl
         if (!rc) rc = upload_proj(m, &D->o, (int)H, qd, o, 1, L);
         if (!rc) rc = upload_proj(m, &D->gu, 2 * c->ffn_dim, (int)H, gu, 2, L);
         if (!rc) rc = upload_proj(m, &D->down, (int)H, c->ffn_dim, dn, 1, L);
+        if (!rc) rc = upload_file_layout(m, &D->down_t, 6, L);
         if (rc) return rc;
         D->in_norm = upload_f32(m, L->in_norm, H);
         D->post_norm = upload_f32(m, L->post_norm, H);
