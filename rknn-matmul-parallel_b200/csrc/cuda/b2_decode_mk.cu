@@ -52,7 +52,8 @@ constexpr int kResCap = 64;        // per-item residual rows prefetched into sha
 constexpr long long kPollLimit = 1ll << 22;
 constexpr long long kBarLimit = 1ll << 22;
 
-enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM, IT_DNT };
+enum { IT_QKV, IT_ATTN, IT_O, IT_GU, IT_DN, IT_LM, IT_DNT, IT_AO, IT_OSEG };
+constexpr int kFuseL = 256;   // contexts up to which attention and o_proj run as one phase
 constexpr int kActCap = 64;   // gate|up channels per CTA (the down partial's inputs)
 
 // Vectors passed between CTAs are "LL" words (the low-latency protocol of
@@ -61,8 +62,10 @@ constexpr int kActCap = 64;   // gate|up channels per CTA (the down partial's in
 // it needs until every tag is this step's, so producers need no fence and no
 // flag, and a consumer starts as soon as its own inputs have landed.
 struct Scratch {
-    unsigned long long* cnt;   // [8 + L]: [0] CTAs finished, [1] best argmax key, [8 + l] down partials of layer l
+    unsigned long long* cnt;   // [8 + 2L]: [0] CTAs finished, [1] best argmax key, [8 + l] down partials of
+                               // layer l, [8 + L + l] attention + o_proj units of layer l
     float* hacc;               // [L][2][H] layer outputs, summed from down partials (two token parities)
+    float* macc;               // [L][2][H] hidden after attention, summed from o_proj partials (fused phase)
     unsigned long long* hbuf;  // LL [L+1][H] layer inputs (row 0 unused: layer 0 reads the embedding)
     unsigned long long* hmid;  // LL [L][H] hidden after attention + residual
     unsigned long long* qkv;   // LL [L][qd + 2 kvd]
@@ -84,8 +87,9 @@ __host__ __device__ inline Scratch scratch_layout(void* base, int L, int H, int 
         off += align256(bytes);
         return r;
     };
-    s.cnt = reinterpret_cast<unsigned long long*>(take((size_t)(8 + L) * 8));
+    s.cnt = reinterpret_cast<unsigned long long*>(take((size_t)(8 + 2 * L) * 8));
     s.hacc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
+    s.macc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
     s.hbuf = reinterpret_cast<unsigned long long*>(take((size_t)(L + 1) * H * 8));
     s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)L * H * 8));
     s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)L * (qd + 2 * kvd) * 8));
@@ -298,6 +302,7 @@ __device__ __forceinline__ int split_lo(int n, int parts, int i) { return (int)(
 
 struct Geo {
     int L, pos, S, G, cta, qd, kvd, nqkv, Gq;
+    int R;  // fused attention + o_proj: o_proj row slices per kv head (0: split attention and o_proj)
 };
 
 struct Chunk {
@@ -307,6 +312,8 @@ struct Chunk {
     const void* src1;
     uint32_t bytes1;
     uint32_t off1;
+    int nseg = 0;            // > 0: nseg copies of bytes0 from src0 + i * seg_stride, packed
+    uint32_t seg_stride = 0;
 };
 
 struct Item {
@@ -339,34 +346,62 @@ __device__ void walk(const B2MkPlan& p, const Geo& geo, V& v) {
             }
             v.end(it);
         }
-        for (int u = geo.cta; u < p.nkv * geo.S && !v.stop(); u += geo.G) {  // attention units
-            const int g = u / geo.S, s = u % geo.S;
-            const int chunk = (geo.L + geo.S - 1) / geo.S;
-            const int p0 = min(geo.L, s * chunk), p1 = min(geo.L, p0 + chunk);
-            const int pc = min(p1, geo.L - 1);  // positions cached by earlier steps
-            Item it{IT_ATTN, l, 0, 0, g, s, p0, p1};
-            v.begin(it);
-            const size_t head = (size_t)l * p.layer_stride + (size_t)g * p.max_seq * kHD;
-            for (int a = p0; a < pc && !v.stop(); a += kStageBytes / (4 * kHD)) {
-                const int b = min(pc, a + kStageBytes / (4 * kHD));
-                const uint32_t bytes = (uint32_t)(b - a) * kHD * 2;
-                Chunk c{IT_ATTN, l, a, b, g, s, p.k_cache + head + (size_t)a * kHD, bytes,
-                        p.v_cache + head + (size_t)a * kHD, bytes, bytes};
-                v.chunk(c);
+        if (geo.R > 0) {  // fused: unit (kv head g, o_proj rows [n0, n1)) = attention of g + its o_proj columns
+            if (geo.cta < p.nkv * geo.R) {
+                const int g = geo.cta / geo.R, r = geo.cta % geo.R;
+                Item it{IT_AO, l, split_lo(H, geo.R, r), split_lo(H, geo.R, r + 1), g, r, 0, geo.L};
+                v.begin(it);
+                const size_t head = (size_t)l * p.layer_stride + (size_t)g * p.max_seq * kHD;
+                for (int a = 0; a < geo.L - 1 && !v.stop(); a += kStageBytes / (4 * kHD)) {
+                    const int b = min(geo.L - 1, a + kStageBytes / (4 * kHD));
+                    const uint32_t bytes = (uint32_t)(b - a) * kHD * 2;
+                    Chunk c{IT_ATTN, l, a, b, g, 0, p.k_cache + head + (size_t)a * kHD, bytes,
+                            p.v_cache + head + (size_t)a * kHD, bytes, bytes};
+                    v.chunk(c);
+                }
+                v.mid(it);
+                // o_proj rows n0..n1, only the columns of kv head g's q heads
+                const uint32_t seg = (uint32_t)row_bytes(WT, geo.Gq * kHD);
+                const int cap = min(64, kStageBytes / (int)seg);
+                for (int a = it.r0; a < it.r1 && !v.stop(); a += cap) {
+                    const int b = min(it.r1, a + cap);
+                    Chunk c{IT_OSEG, l, a, b, g, 0, (const unsigned char*)Lw.o + a * rb_q + (size_t)g * seg, seg,
+                            nullptr, 0, 0, b - a, (uint32_t)rb_q};
+                    v.chunk(c);
+                }
+                v.end(it);
             }
-            v.end(it);
-        }
-        if (v.stop()) return;
-        {  // o_proj rows
-            Item it{IT_O, l, split_lo(H, geo.G, geo.cta), split_lo(H, geo.G, geo.cta + 1), 0, 0, 0, 0};
-            v.begin(it);
-            for (int a = it.r0; a < it.r1 && !v.stop(); a += cap_q) {
-                const int b = min(it.r1, a + cap_q);
-                Chunk c{IT_O, l, a, b, 0, 0, (const unsigned char*)Lw.o + a * rb_q, (uint32_t)((b - a) * rb_q),
-                        nullptr, 0, 0};
-                v.chunk(c);
+        } else {
+            for (int u = geo.cta; u < p.nkv * geo.S && !v.stop(); u += geo.G) {  // attention units
+                const int g = u / geo.S, s = u % geo.S;
+                const int chunk = (geo.L + geo.S - 1) / geo.S;
+                const int p0 = min(geo.L, s * chunk), p1 = min(geo.L, p0 + chunk);
+                const int pc = min(p1, geo.L - 1);  // positions cached by earlier steps
+                Item it{IT_ATTN, l, 0, 0, g, s, p0, p1};
+                v.begin(it);
+                const size_t head = (size_t)l * p.layer_stride + (size_t)g * p.max_seq * kHD;
+                for (int a = p0; a < pc && !v.stop(); a += kStageBytes / (4 * kHD)) {
+                    const int b = min(pc, a + kStageBytes / (4 * kHD));
+                    const uint32_t bytes = (uint32_t)(b - a) * kHD * 2;
+                    Chunk c{IT_ATTN, l, a, b, g, s, p.k_cache + head + (size_t)a * kHD, bytes,
+                            p.v_cache + head + (size_t)a * kHD, bytes, bytes};
+                    v.chunk(c);
+                }
+                v.end(it);
             }
-            v.end(it);
+            if (v.stop()) return;
+            {  // o_proj rows
+                Item it{IT_O, l, split_lo(H, geo.G, geo.cta), split_lo(H, geo.G, geo.cta + 1), 0, 0, 0, 0};
+                v.begin(it);
+                for (int a = it.r0; a < it.r1 && !v.stop(); a += cap_q) {
+                    const int b = min(it.r1, a + cap_q);
+                    Chunk c{IT_O, l, a, b, 0, 0, (const unsigned char*)Lw.o + a * rb_q, (uint32_t)((b - a) * rb_q),
+                            nullptr, 0, 0};
+                    v.chunk(c);
+                }
+                v.end(it);
+            }
+            if (v.stop()) return;
         }
         if (v.stop()) return;
         {  // gate|up channel pairs, then the same channels' rows of the input-major down weight
@@ -439,6 +474,7 @@ struct Producer {
         return dead || *(volatile const int*)&sh.abort || *(volatile const int*)&sh.cabort;
     }
     __device__ void begin(const Item&) {}
+    __device__ void mid(const Item&) {}
     __device__ void end(const Item&) {}
     __device__ void chunk(const Chunk& c) {
         const int stage = n % kStages;
@@ -458,9 +494,16 @@ struct Producer {
             }
         }
         unsigned char* dst = ring + (size_t)stage * kStageBytes;
-        mbar_expect_tx(&sh.full[stage], c.bytes0 + c.bytes1);
-        bulk_g2s(dst, c.src0, c.bytes0, &sh.full[stage]);
-        if (c.bytes1) bulk_g2s(dst + c.off1, c.src1, c.bytes1, &sh.full[stage]);
+        if (c.nseg > 0) {  // row segments, packed back to back
+            mbar_expect_tx(&sh.full[stage], (uint32_t)c.nseg * c.bytes0);
+            for (int i = 0; i < c.nseg; i++)
+                bulk_g2s(dst + (size_t)i * c.bytes0, (const unsigned char*)c.src0 + (size_t)i * c.seg_stride, c.bytes0,
+                         &sh.full[stage]);
+        } else {
+            mbar_expect_tx(&sh.full[stage], c.bytes0 + c.bytes1);
+            bulk_g2s(dst, c.src0, c.bytes0, &sh.full[stage]);
+            if (c.bytes1) bulk_g2s(dst + c.off1, c.src1, c.bytes1, &sh.full[stage]);
+        }
         n++;
         *(volatile int*)&sh.issued = n;
     }
@@ -587,6 +630,9 @@ struct Consumer {
         aborted = *(volatile int*)&sh.cabort != 0;
     }
     __device__ unsigned long long* dn_count(int l) const { return S.cnt + 8 + l; }
+    __device__ unsigned long long* ao_count(int l) const { return S.cnt + 8 + p.n_layers + l; }
+    __device__ float* mid_acc(int l) const { return S.macc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
+    __device__ int ao_units() const { return p.nkv * (geo.G / p.nkv); }
     // output of layer l (input of layer l + 1) for this step's parity
     __device__ float* layer_out(int l) const { return S.hacc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
     // groups of a vector summed by other CTAs in this launch: read through L2
@@ -780,6 +826,12 @@ struct Consumer {
                 if (!stop()) stage(v, H, Lw.in_norm, perm);
                 break;
             case IT_ATTN: attn_prologue(it); break;
+            case IT_AO:
+                isc = Lw.o_s;
+                load_scales(Lw.o_s, 0);
+                if (it.g == 0) load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1));
+                attn_prologue(it);
+                break;
             case IT_O:
                 isc = Lw.o_s;
                 load_scales(Lw.o_s, 0);
@@ -792,7 +844,13 @@ struct Consumer {
                 isc = Lw.gu_s;
                 load_scales(Lw.gu_s, p.ffn);
                 load_norm(Lw.post_norm, H);
-                ok = ll_gather(S.hmid + (size_t)it.l * H, H, v);
+                if (geo.R > 0) {
+                    wait_counter(ao_count(it.l), (unsigned long long)ao_units() * tag);
+                    if (stop()) return;
+                    cg_gather(mid_acc(it.l), H, v);
+                } else {
+                    ok = ll_gather(S.hmid + (size_t)it.l * H, H, v);
+                }
 #pragma unroll
                 for (int i = 0; i < 4; i++) dacc_[i] = 0.f;
                 res4_ = v[0];  // CTA 0 adds hmid (outputs 4 tid ..) into the layer output
@@ -812,6 +870,11 @@ struct Consumer {
                 best = 0ull;
                 break;
         }
+    }
+
+    __device__ void mid(const Item& it) {
+        if (stop()) return;
+        if (it.type == IT_AO) attn_to_xs(it);
     }
 
     // Every consumer waits for the stage itself (so the bulk-copied bytes are
@@ -844,6 +907,7 @@ struct Consumer {
             case IT_O: rows_resid(c, buf_, geo.qd); break;
             case IT_GU: rows_gu(c, buf_); break;
             case IT_DNT: rows_dnt(c, buf_); break;
+            case IT_OSEG: rows_oseg(c, buf_); break;
             case IT_LM: rows_lm(c, buf_); break;
         }
         __syncwarp();  // this warp is done reading the stage
@@ -858,6 +922,12 @@ struct Consumer {
         if (stop()) return;
         if (it.type == IT_ATTN) {
             attn_epilogue(it);
+        } else if (it.type == IT_AO) {
+            consumer_sync();  // every consumer's o_proj additions precede the release
+            if (tid == 0) red_release(ao_count(it.l), 1ull);
+        } else if (it.type == IT_O) {
+            // split phase: keep the fused phase's counter in step (one unit count per step)
+            if (geo.cta == 0 && tid == 0) red_release(ao_count(it.l), (unsigned long long)ao_units());
         } else if (it.type == IT_GU) {
             // this CTA's down partial (its gate|up channels) into the layer
             // output; CTA 0 also adds the residual hmid.  The barrier orders
@@ -990,6 +1060,22 @@ struct Consumer {
         }
     }
 
+    // Fused phase: o_proj rows [c.a, c.b) restricted to kv head c.g's columns,
+    // times the unit's attention output; the partial (plus the residual, from
+    // kv head 0's units) is added into this step's hidden-after-attention.
+    __device__ void rows_oseg(const Chunk& c, const unsigned char* buf_) {
+        const int K = geo.Gq * kHD;
+        const size_t rb = row_bytes(WT, K);
+        const int n = c.b - c.a;
+        const float v = chunk_dot<WT>(n, K, [&](int r) { return buf_ + (size_t)r * rb; });
+        if (tid < n) {
+            const int r = c.a + tid;
+            float y = v * scale(isc, r - r0, 0);
+            if (c.g == 0) y += resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0);
+            atomicAdd(mid_acc(c.l) + r, y);
+        }
+    }
+
     // CTA 0: the final residual stream (before the final norm) for the host.
     __device__ void write_final(const float4 (&v)[kV]) const {
 #pragma unroll
@@ -1099,7 +1185,7 @@ struct Consumer {
 #pragma unroll
             for (int j = 0; j < 4; j++) dst[e0 + j] = x[j];
             // The unit covering the newest position stores its K and V.
-            if (h >= Gq && it.p1 == geo.L && it.p0 <= geo.L - 1) {
+            if (h >= Gq && it.p1 == geo.L && it.p0 <= geo.L - 1 && (it.type != IT_AO || it.s == 0)) {
                 uint16_t* base = (h == Gq ? p.k_cache : p.v_cache) + (size_t)it.l * p.layer_stride +
                                  ((size_t)it.g * p.max_seq + geo.pos) * kHD;
                 __half* d16 = reinterpret_cast<__half*>(base);
@@ -1170,7 +1256,9 @@ struct Consumer {
         }
     }
 
-    __device__ void attn_epilogue(const Item& it) {
+    // Fold the newest position into the softmax state, merge the lane groups
+    // of each warp, and leave one (m, l, o) state per warp in shared memory.
+    __device__ void attn_merge_warps(const Item& it) {
         const int Gq = geo.Gq, sub = lane & 7;
         // the newest position (not in the cache stream): lane group 0 of warp 0
         if (it.p1 == geo.L && it.p0 <= geo.L - 1 && warp == 0) {
@@ -1214,20 +1302,45 @@ struct Consumer {
             }
         }
         consumer_sync();
-        // merge the per-warp states into this unit's partial (thread = (head, dim))
+    }
+
+    // merged (m, l, o) of head h, dim d over the warps' states
+    __device__ void attn_state(int h, int d, float& M, float& ls, float& acc) const {
+        M = -INFINITY;
+        for (int r = 0; r < kCWarps; r++) M = fmaxf(M, sh.gm[r][h]);
+        ls = 0.f;
+        acc = 0.f;
+        if (M != -INFINITY)
+            for (int r = 0; r < kCWarps; r++) {
+                if (sh.gm[r][h] == -INFINITY) continue;
+                const float w = expf(sh.gm[r][h] - M);
+                ls = fmaf(sh.gl[r][h], w, ls);
+                acc = fmaf(sh.go[r][h][d], w, acc);
+            }
+    }
+
+    // Fused phase: the attention output of the unit's q heads, FP16-rounded,
+    // as the staged input of its o_proj columns (k order of sb_mma).
+    __device__ void attn_to_xs(const Item& it) {
+        attn_merge_warps(it);
+        for (int t = tid; t < geo.Gq * kHD; t += kConsumers) {
+            float M, ls, acc;
+            attn_state(t / kHD, t % kHD, M, ls, acc);
+            const int pos = WT == B2_W_I4 ? (t & ~7) + ((t & 7) < 4 ? 2 * (t & 7) : 2 * ((t & 7) - 4) + 1) : t;
+            xs[pos] = __float2half_rn(acc / ls);
+        }
+        consumer_sync();
+    }
+
+    // Split phase: write this unit's partial (m, l, o) for o_proj's combine.
+    __device__ void attn_epilogue(const Item& it) {
+        const int Gq = geo.Gq;
+        attn_merge_warps(it);
         const size_t unit = (((size_t)it.l * p.nkv + it.g) * kMaxSplit + it.s) * Gq;
         for (int t = tid; t < Gq * kHD; t += kConsumers) {
             const int h = t / kHD, d = t % kHD;
-            float M = -INFINITY;
-            for (int r = 0; r < kCWarps; r++) M = fmaxf(M, sh.gm[r][h]);
-            float ls = 0.f, acc = 0.f;
-            if (M != -INFINITY)
-                for (int r = 0; r < kCWarps; r++) {
-                    if (sh.gm[r][h] == -INFINITY) continue;
-                    const float w = expf(sh.gm[r][h] - M);
-                    ls = fmaf(sh.gl[r][h], w, ls);
-                    acc = fmaf(sh.go[r][h][d], w, acc);
-                }
+            float M, ls, acc;
+            attn_state(h, d, M, ls, acc);
             unsigned long long* rec = S.part + (unit + h) * (2 + kHD);
             ll_put(rec + 2 + d, acc, tag);
             if (d == 0) {
@@ -1275,6 +1388,10 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
         const int cap = min(kMaxSplit, max(1, geo.G / p.nkv));
         geo.S = max(1, min(s, cap));
     }
+    // fused attention + o_proj while every unit's o_proj slice fits the prefetch buffers
+    geo.R = (geo.L <= kFuseL && geo.G >= p.nkv && (p.hidden + geo.G / p.nkv - 1) / (geo.G / p.nkv) <= kResCap)
+                ? geo.G / p.nkv
+                : 0;
     const unsigned long long gen = (unsigned long long)(unsigned)p.state[B2_MK_GEN];
 
     if (warp == kCWarps) {
@@ -1293,8 +1410,12 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
             const int total = p.n_layers * per;
             const int a = split_lo(total, geo.G, geo.cta), b = split_lo(total, geo.G, geo.cta + 1);
             const unsigned npar = (unsigned)(gen + 2) & 1u;
-            for (int i = a + tid; i < b; i += kConsumers)
-                z[((size_t)(i / per) * 2 + npar) * per + (i % per)] = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4* zm = reinterpret_cast<float4*>(S.macc);
+            for (int i = a + tid; i < b; i += kConsumers) {
+                const size_t o = ((size_t)(i / per) * 2 + npar) * per + (i % per);
+                z[o] = make_float4(0.f, 0.f, 0.f, 0.f);
+                zm[o] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
         walk<WT>(p, geo, cons);
         if (!p.do_lm && geo.cta == 0 && !cons.stop()) {  // prefill-mode step: publish the final hidden
