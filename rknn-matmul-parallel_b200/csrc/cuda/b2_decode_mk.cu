@@ -276,20 +276,32 @@ __device__ __forceinline__ void tile_dot(const unsigned char* rg, const unsigned
                                          int s0, int s1, int lane, float (&out)[2]) {
     constexpr int XW = sb_k<WT>() / 8;  // activation words (half2) per lane per super-block
     const int q = lane & 3;
+    // four accumulators (FP16 / INT8): consecutive super-blocks use different
+    // pairs, so a warp's dependent MMA chains are a quarter of its MMAs long
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-    for (int sb = s0; sb < s1; sb++) {
+    float d2[4] = {0.f, 0.f, 0.f, 0.f}, d3[4] = {0.f, 0.f, 0.f, 0.f};
+    auto step = [&](int sb, float (&da)[4], float (&db)[4]) {
         const uint4 wg = *reinterpret_cast<const uint4*>(rg + sb * 64 + q * 16);
         const uint4 wh = *reinterpret_cast<const uint4*>(rh + sb * 64 + q * 16);
         uint32_t xw[XW];
         const uint4* xp = reinterpret_cast<const uint4*>(xs + sb * sb_k<WT>() + q * (sb_k<WT>() / 4));
 #pragma unroll
         for (int i = 0; i < XW / 4; i++) *reinterpret_cast<uint4*>(xw + 4 * i) = xp[i];
-        sb_mma<WT>(d0, d1, wg, wh, xw);
+        sb_mma<WT>(da, db, wg, wh, xw);
+    };
+    int sb = s0;
+    if constexpr (WT == B2_W_I4) {  // eight MMAs per super-block already; two accumulators keep registers
+        for (; sb < s1; sb++) step(sb, d0, d1);
+    } else {
+        for (; sb + 1 < s1; sb += 2) {
+            step(sb, d0, d1);
+            step(sb + 1, d2, d3);
+        }
+        if (sb < s1) step(sb, d0, d1);
     }
     // all 8 columns hold the same sums: column 2q of rows g and g + 8
-    out[0] = d0[0] + d1[0];
-    out[1] = d0[2] + d1[2];
+    out[0] = (d0[0] + d1[0]) + (d2[0] + d3[0]);
+    out[1] = (d0[2] + d1[2]) + (d2[2] + d3[2]);
 }
 
 __host__ __device__ inline size_t row_bytes(int wtype, int K) {
