@@ -90,7 +90,12 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     b->max_seq = max_seq_len;
     int sm = 148;
     b2_sm_count(&sm);
-    b->split = (2 * sm + n_seqs * cfg.num_kv_heads - 1) / (n_seqs * cfg.num_kv_heads);
+    /* attention position ranges per (sequence, kv head): about eight CTAs per
+     * SM, so the long sequences do not leave a tail of idle SMs
+     * (B2_BATCH_SPLIT overrides) */
+    b->split = (8 * sm + n_seqs * cfg.num_kv_heads - 1) / (n_seqs * cfg.num_kv_heads);
+    const char* es = getenv("B2_BATCH_SPLIT");
+    if (es && atoi(es) > 0) b->split = atoi(es);
     if (b->split < 1) b->split = 1;
     if (b->split > 64) b->split = 64;
     b2_get_device(&b->device);
