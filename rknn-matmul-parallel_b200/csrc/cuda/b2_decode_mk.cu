@@ -40,8 +40,8 @@ namespace {
 constexpr int kCWarps = 8;
 constexpr int kConsumers = kCWarps * 32;
 constexpr int kThreads = kConsumers + 32;
-constexpr int kStages = 6;
-constexpr int kStageBytes = 32 * 1024;
+constexpr int kStages = 3;
+constexpr int kStageBytes = 64 * 1024;
 constexpr int kHD = 128;
 constexpr int kMaxK = 3072;        // longest staged activation (hidden, q_dim, ffn)
 constexpr int kV = kMaxK / (4 * kConsumers);  // float4 groups of a staged vector per consumer thread
