@@ -173,6 +173,14 @@ int b2_qk_rope_kv(float* qkv, int ldqkv, int M, int nq, int nkv, int hd,
                   const float* cos_tab, const float* sin_tab, int rope_style,
                   const B2KVRef* kv, b2_stream_t s);
 
+/* Causal flash attention of M consecutive rows of one sequence at positions
+ * base .. base + M - 1 whose K and V are already stored: row m attends cache
+ * positions [0, base + m].  Same inputs and output layout as b2_attention
+ * (kv->rows_seq must be NULL, head_dim 128, nq = 2 nkv); scores and P.V run
+ * on the tensor cores with FP16 Q and P and FP32 accumulation and softmax. */
+int b2_attention_prefill(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                         const B2KVRef* kv, int base, b2_stream_t s);
+
 /* GQA attention of row m over cache positions [0, pos[m]] (inclusive).
  * q device FP32 [M][ldq] (first nq*hd), out device FP32 [M][nq*hd].
  * work: device scratch of at least b2_attention_workspace(M, nq, hd, nsplit)

@@ -201,7 +201,7 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
     if (!rc) rc = b2_embed(b->hidden, m->emb, b->d_blk, NULL, NULL, n, H, s);
     B2KVRef kv = {b->k_cache, b->v_cache, b->seq_stride, b->layer_stride, 0, b->max_seq, b->d_blk + 2 * n,
                   b->d_blk + n, n};
-    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16};
+    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16, -1};
     if (!rc) rc = md_enqueue_layers(m, &lb, n, &kv, s);
     if (!rc) rc = b2_event_record(b->ev[1], s);
     if (!rc && b->x16 && n >= 16 && (m->lm_wtype == B2_W_I8 || m->lm_wtype == B2_W_F16) && H % 64 == 0) {

@@ -7,7 +7,8 @@
  * plus the attention combine:
  *   1. RMSNorm(input_norm) + fused q|k|v GEMV                       (b2_gemv)
  *   2. per-head q/k RMSNorm + RoPE + K/V store at pos              (b2_qk_rope_kv)
- *   3. GQA attention over [0, pos] (split-KV + combine)            (b2_attention)
+ *   3. GQA attention over [0, pos] (split-KV + combine)            (b2_attention;
+ *      causal flash attention b2_attention_prefill for prefill rows)
  *   4. o_proj GEMV + residual add into hidden                       (b2_gemv ADD)
  *   5. RMSNorm(post_attn_norm) + gate|up GEMV + SiLU*mul            (b2_gemv SILU_PAIR)
  *   6. down GEMV + residual add into hidden                         (b2_gemv ADD)
@@ -67,7 +68,10 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         rc = b2_qk_rope_kv(b->qkv, ldqkv, M, nq, nkv, hd, qk ? L->q_norm : NULL, qk ? L->k_norm : NULL,
                            c->rms_eps, m->cos_tab, m->sin_tab, c->rope_style, &kv, s);
         if (rc) return rc;
-        rc = b2_attention(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
+        if (b->prefill_base >= 0 && M >= MD_GEMM_MIN_ROWS && nq == 2 * nkv && hd == 128 && !kv.rows_seq)
+            rc = b2_attention_prefill(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->prefill_base, s);
+        else
+            rc = b2_attention(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
         if (rc) return rc;
         B2GemvArgs o = {b->hidden, H, b->attn, qd, M, qd, H, L->o.w, L->o.s, L->o.wtype, NULL, 0.f,
                         B2_EPI_ADD};

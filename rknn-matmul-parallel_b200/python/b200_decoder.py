@@ -127,6 +127,7 @@ SIGNATURES = {
     "b2_graph_destroy": (c_int, [c_vp]),
     "b2_gemv": (c_int, [c_vp, c_vp]),
     "b2_gemm": (c_int, [c_vp, c_vp]),
+    "b2_attention_prefill": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp]),
     "b2_gemm_argmax_keys": (ctypes.c_size_t, [c_int, c_int]),
     "b2_rows_to_f16": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_int, c_vp, c_float, c_vp]),
     "b2_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),

@@ -385,6 +385,43 @@ def test_attention_rows_and_sequences(G):
             assert_close(out[m], exp, rtol=1e-3, atol=1e-4)
 
 
+@pytest.mark.parametrize("M, base", [(16, 0), (60, 0), (77, 100), (512, 0), (200, 3000)])
+def test_attention_prefill_flash_matches_oracle(M, base):
+    """Causal flash attention of a prefill chunk (tensor cores, FP16 Q and P)
+    against the oracle's FP32 attention on sampled rows, and against the
+    per-row split kernel on every row."""
+    nkv, hd, G = 8, 128, 2
+    nq, max_seq = nkv * G, base + M + 4
+    rng = np.random.default_rng(7000 + M + base)
+    kc = rng.standard_normal((nkv, max_seq, hd), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((nkv, max_seq, hd), dtype=np.float32).astype(np.float16)
+    q = rng.standard_normal((M, nq * hd), dtype=np.float32)
+    pos = (base + np.arange(M)).astype(np.int32)
+    kc_d, vc_d, q_d = dev(kc), dev(vc), dev(q)
+    kv = kv_ref(kc_d, vc_d, 0, max_seq, dev(pos))
+    out_f = torch.empty((M, nq * hd), dtype=torch.float32, device=DEV)
+    bd.check(bd.capi().b2_attention_prefill(out_f.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
+                                            ctypes.byref(kv), base, stream()), "attention_prefill")
+    work = torch.empty(bd.capi().b2_attention_workspace(M, nq, hd, 0), dtype=torch.uint8, device=DEV)
+    out_s = torch.empty((M, nq * hd), dtype=torch.float32, device=DEV)
+    bd.check(bd.capi().b2_attention(out_s.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd, ctypes.byref(kv),
+                                    work.data_ptr(), 0, stream()), "attention")
+    torch.cuda.synchronize()
+    flash, split = out_f.cpu().numpy(), out_s.cpu().numpy()
+    assert_close(flash, split, rtol=2e-2, atol=5e-3)
+    for m in sorted({0, M // 3, M - 1}):
+        L = base + m + 1
+        exp = ref.attention(q[m], kc[:, :L].transpose(1, 0, 2).astype(np.float32),
+                            vc[:, :L].transpose(1, 0, 2).astype(np.float32), nq, nkv, hd)
+        assert_close(flash[m], exp, rtol=2e-2, atol=5e-3)
+
+
+def test_attention_prefill_rejects_unsupported():
+    kv = bd.B2KVRef(16, 16, 0, 0, 0, 64, None, 16, 1)
+    assert bd.capi().b2_attention_prefill(16, 16, 2048, 8, 24, 8, 128, ctypes.byref(kv), 0, None) == -1  # G = 3
+    assert bd.capi().b2_attention_prefill(16, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 60, None) == -1  # past max_seq
+
+
 def lm_reference(x, norm_w, table, scales, wtype):
     xn = ref.rms_norm(x, norm_w)
     if wtype == bd.W_I8:
