@@ -136,6 +136,8 @@ typedef struct {
     int epilogue;
     unsigned long long* keys;
     int* tokens;
+    uint16_t* y16; /* STORE / SILU_PAIR: when not NULL, the output as FP16 rows
+                      (stride ldy) instead of y, e.g. the next GEMM's x16 */
 } B2GemmArgs;
 size_t b2_gemm_argmax_keys(int M, int N);
 int b2_gemm(const B2GemmArgs* a, b2_stream_t s);
@@ -177,8 +179,10 @@ int b2_qk_rope_kv(float* qkv, int ldqkv, int M, int nq, int nkv, int hd,
  * base .. base + M - 1 whose K and V are already stored: row m attends cache
  * positions [0, base + m].  Same inputs and output layout as b2_attention
  * (kv->rows_seq must be NULL, head_dim 128, nq = 2 nkv); scores and P.V run
- * on the tensor cores with FP16 Q and P and FP32 accumulation and softmax. */
-int b2_attention_prefill(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
+ * on the tensor cores with FP16 Q and P and FP32 accumulation and softmax.
+ * With out16 (not NULL) the output is written as FP16 [M][nq*hd] instead of
+ * out: the o_proj GEMM's input rows. */
+int b2_attention_prefill(float* out, uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
                          const B2KVRef* kv, int base, b2_stream_t s);
 
 /* GQA attention of row m over cache positions [0, pos[m]] (inclusive).
@@ -188,6 +192,9 @@ int b2_attention_prefill(float* out, const float* q, int ldq, int M, int nq, int
 size_t b2_attention_workspace(int M, int nq, int hd, int nsplit);
 int b2_attention(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
                  const B2KVRef* kv, void* work, int nsplit, b2_stream_t s);
+/* b2_attention writing FP16 [M][nq*hd] rows (the o_proj GEMM's input). */
+int b2_attention_f16(uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                     const B2KVRef* kv, void* work, int nsplit, b2_stream_t s);
 
 /* lm_head + argmax over V rows of `table` (int8 [V][K] with FP32 scales,
  * F16 [V][K], or F32 [V][K]).  Input row m is RMSNorm(x[m]; norm_w, eps)

@@ -167,8 +167,8 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(const float* __res
     }
 }
 
-__global__ void __launch_bounds__(kHD) attn_combine_kernel(float* __restrict__ out, int nq,
-                                                           const float* __restrict__ part_ml,
+__global__ void __launch_bounds__(kHD) attn_combine_kernel(float* __restrict__ out, __half* __restrict__ out16,
+                                                           int nq, const float* __restrict__ part_ml,
                                                            const float* __restrict__ part_o, int nsplit) {
     b2::pdl_trigger();
     b2::pdl_wait();
@@ -184,7 +184,8 @@ __global__ void __launch_bounds__(kHD) attn_combine_kernel(float* __restrict__ o
         den = fmaf(part_ml[(base + s) * 2 + 1], w, den);
         num = fmaf(part_o[(base + s) * kHD + d], w, num);
     }
-    out[((size_t)m * nq + h) * kHD + d] = num / den;
+    if (out16) out16[((size_t)m * nq + h) * kHD + d] = __float2half_rn(num / den);
+    else out[((size_t)m * nq + h) * kHD + d] = num / den;
 }
 
 int pick_split(int M, int nkv, int nsplit) {
@@ -201,11 +202,11 @@ extern "C" size_t b2_attention_workspace(int M, int nq, int hd, int nsplit) {
     return (size_t)M * nq * nsplit * (2 + kHD) * sizeof(float) + 256;
 }
 
-extern "C" int b2_attention(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
-                            const B2KVRef* kv, void* work, int nsplit, b2_stream_t s) {
+static int attention_impl(float* out, __half* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                          const B2KVRef* kv, void* work, int nsplit, b2_stream_t s) {
     if (M <= 0) return 0;
     if (hd != kHD) return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention: head_dim %d != 128", hd);
-    if (!out || !q || !kv || !kv->pos || !work || nkv <= 0 || nq % nkv != 0)
+    if ((!out && !out16) || !q || !kv || !kv->pos || !work || nkv <= 0 || nq % nkv != 0)
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention: bad arguments");
     nsplit = pick_split(M, nkv, nsplit);
     float* part_ml = reinterpret_cast<float*>(work);
@@ -220,10 +221,20 @@ extern "C" int b2_attention(float* out, const float* q, int ldq, int M, int nq, 
         default: return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention: GQA group %d not in {1,2,4}", nq / nkv);
     }
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention split: %s", cudaGetErrorString(e));
-    e = b2::launch_pdl(attn_combine_kernel, dim3(nq, M), dim3(kHD), 0, st, out, nq, (const float*)part_ml,
+    e = b2::launch_pdl(attn_combine_kernel, dim3(nq, M), dim3(kHD), 0, st, out, out16, nq, (const float*)part_ml,
                        (const float*)part_o, nsplit);
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention combine: %s", cudaGetErrorString(e));
     return 0;
+}
+
+extern "C" int b2_attention(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                            const B2KVRef* kv, void* work, int nsplit, b2_stream_t s) {
+    return attention_impl(out, nullptr, q, ldq, M, nq, nkv, hd, kv, work, nsplit, s);
+}
+
+extern "C" int b2_attention_f16(uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                                const B2KVRef* kv, void* work, int nsplit, b2_stream_t s) {
+    return attention_impl(nullptr, reinterpret_cast<__half*>(out16), q, ldq, M, nq, nkv, hd, kv, work, nsplit, s);
 }
 
 // ─── causal flash attention for batch prefill (b2_attention_prefill) ───
@@ -278,8 +289,9 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __restrict__ out, const float* __restrict__ q,
-                                                                   int ldq, int M, int nq, B2KVRef kv, int base) {
+__global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __restrict__ out, __half* __restrict__ out16,
+                                                                   const float* __restrict__ q, int ldq, int M, int nq,
+                                                                   B2KVRef kv, int base) {
     static_assert(G * kFaRows == 64, "four warps of 16 query rows");
     extern __shared__ __align__(16) unsigned char fsm[];
     __half* sq = reinterpret_cast<__half*>(fsm);                 // [64][kFaPad]
@@ -428,21 +440,24 @@ __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __rest
 #pragma unroll
     for (int j = 0; j < kHD / 8; j++) {
         const int d = j * 8 + 2 * q4;
-        if (m0 + tA < M)
-            *reinterpret_cast<float2*>(out + (size_t)(m0 + tA) * nq * kHD + (size_t)(g * G + hA) * kHD + d) =
-                make_float2(o[j][0] * iA, o[j][1] * iA);
-        if (m0 + tB < M)
-            *reinterpret_cast<float2*>(out + (size_t)(m0 + tB) * nq * kHD + (size_t)(g * G + hB) * kHD + d) =
-                make_float2(o[j][2] * iB, o[j][3] * iB);
+        const size_t oA = (size_t)(m0 + tA) * nq * kHD + (size_t)(g * G + hA) * kHD + d;
+        const size_t oB = (size_t)(m0 + tB) * nq * kHD + (size_t)(g * G + hB) * kHD + d;
+        if (out16) {  // FP16 rows for the o_proj GEMM
+            if (m0 + tA < M) *reinterpret_cast<__half2*>(out16 + oA) = __floats2half2_rn(o[j][0] * iA, o[j][1] * iA);
+            if (m0 + tB < M) *reinterpret_cast<__half2*>(out16 + oB) = __floats2half2_rn(o[j][2] * iB, o[j][3] * iB);
+        } else {
+            if (m0 + tA < M) *reinterpret_cast<float2*>(out + oA) = make_float2(o[j][0] * iA, o[j][1] * iA);
+            if (m0 + tB < M) *reinterpret_cast<float2*>(out + oB) = make_float2(o[j][2] * iB, o[j][3] * iB);
+        }
     }
 }
 
 }  // namespace
 
-extern "C" int b2_attention_prefill(float* out, const float* q, int ldq, int M, int nq, int nkv, int hd,
-                                    const B2KVRef* kv, int base, b2_stream_t s) {
+extern "C" int b2_attention_prefill(float* out, uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv,
+                                    int hd, const B2KVRef* kv, int base, b2_stream_t s) {
     if (M <= 0) return 0;
-    if (hd != kHD || !out || !q || !kv || nkv <= 0 || nq != 2 * nkv || base < 0 || base + M > kv->max_seq ||
+    if (hd != kHD || (!out && !out16) || !q || !kv || nkv <= 0 || nq != 2 * nkv || base < 0 || base + M > kv->max_seq ||
         ldq % 4 || kv->rows_seq)
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_prefill: needs hd 128, GQA group 2, one sequence");
     const size_t smem = (size_t)(64 + 4 * kFaKv) * kFaPad * sizeof(__half);
@@ -454,8 +469,8 @@ extern "C" int b2_attention_prefill(float* out, const float* q, int ldq, int M, 
         configured = 1;
     }
     const dim3 grid((M + kFaRows - 1) / kFaRows, nkv);
-    cudaError_t e = b2::launch_pdl(flash_prefill_kernel<2>, grid, dim3(kFaThreads), smem, (cudaStream_t)s, out, q, ldq,
-                                   M, nq, *kv, base);
+    cudaError_t e = b2::launch_pdl(flash_prefill_kernel<2>, grid, dim3(kFaThreads), smem, (cudaStream_t)s, out,
+                                   reinterpret_cast<__half*>(out16), q, ldq, M, nq, *kv, base);
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention_prefill: %s", cudaGetErrorString(e));
     return 0;
 }

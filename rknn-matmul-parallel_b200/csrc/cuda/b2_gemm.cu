@@ -68,6 +68,7 @@ struct GemmParams {
     const float* scales;
     int epilogue;
     unsigned long long* keys;  // ARGMAX: [M][gridDim.x] per-CTA keys
+    __half* y16;               // STORE / SILU_PAIR: FP16 output (row stride ldy) instead of y
 };
 
 struct Bars {
@@ -313,6 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; j++)
                         if (j < jn) yp[(size_t)j * g.ldy] = old[j] + __uint_as_float(v[j]) * sc;
+                } else if (g.y16) {
+                    __half* hp = g.y16 + (size_t)(m0 + c0) * g.ldy + n;
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < jn) hp[(size_t)j * g.ldy] = __float2half_rn(__uint_as_float(v[j]) * sc);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; j++)
@@ -329,13 +335,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + BN + c0, vu);
                 const int jn = min(16, g.M - (m0 + c0));
                 if (jn <= 0) break;
-                float* yp = g.y + (size_t)(m0 + c0) * g.ldy + n;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     if (j >= jn) break;
                     const float gv = __uint_as_float(vg[j]) * sg, uv = __uint_as_float(vu[j]) * su;
                     const float sig = 1.0f / (1.0f + expf(-gv));
-                    yp[(size_t)j * g.ldy] = (gv * sig) * uv;
+                    const size_t o = (size_t)(m0 + c0 + j) * g.ldy + n;
+                    if (g.y16) g.y16[o] = __float2half_rn((gv * sig) * uv);  // the down GEMM's FP16 input
+                    else g.y[o] = (gv * sig) * uv;
                 }
             }
         } else {  // ARGMAX over this CTA's 128 vocab rows, per token
@@ -479,7 +486,8 @@ int launch(const B2GemmArgs* a, cudaStream_t s, int sms) {
     cudaError_t e = cudaSuccess;
     std::call_once(once[dev & 7], [&] { e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm smem attr: %s", cudaGetErrorString(e));
-    GemmParams g{a->y, a->ldy, a->M, a->K, a->N, a->scales, a->epilogue, a->keys};
+    GemmParams g{a->y, a->ldy, a->M, a->K, a->N, a->scales, a->epilogue, a->keys,
+                 reinterpret_cast<__half*>(a->y16)};
     const int gx = (a->N + kBM - 1) / kBM, gy = (a->M + BN - 1) / BN;
     // A residual-add GEMM whose grid leaves SMs idle splits K over more CTAs
     // (each adds its partial sum into y; at least 4 k stages per split).
@@ -520,11 +528,12 @@ extern "C" int b2_gemm(const B2GemmArgs* a, b2_stream_t stream) {
     if (a->M == 0) return 0;
     const int epi = a->epilogue;
     const bool argmax = epi == B2_EPI_ARGMAX;
-    if (epi < B2_EPI_STORE || epi > B2_EPI_ARGMAX || (!argmax && !a->y) || (argmax && (!a->keys || !a->tokens)))
+    if (epi < B2_EPI_STORE || epi > B2_EPI_ARGMAX || (!argmax && !a->y && !a->y16) ||
+        (a->y16 && epi != B2_EPI_STORE && epi != B2_EPI_SILU_PAIR) || (argmax && (!a->keys || !a->tokens)))
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_gemm: missing output for epilogue %d", epi);
     if ((a->wtype != B2_W_F16 && a->wtype != B2_W_I8 && a->wtype != B2_W_I4) ||
         (a->wtype != B2_W_F16 && !a->scales) || a->K % kBK || (!argmax && a->N % kBM) || a->ldx % 8 ||
-        a->ldx < a->K || (a->y && a->ldy < a->N) || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
+        a->ldx < a->K || ((a->y || a->y16) && a->ldy < a->N) || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
         (reinterpret_cast<uintptr_t>(a->w) & 15))
         return b2_set_error(B2_ERR_INVALID_ARG,
                             "b2_gemm: needs F16/I8/I4 weights (scales for I8/I4), K %% 64 == 0, N %% 128 == 0, "

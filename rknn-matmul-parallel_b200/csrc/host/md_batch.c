@@ -25,6 +25,7 @@ struct MatmulDecoderBatch {
     long long seq_stride, layer_stride;
     float *hidden, *qkv, *attn, *act, *logits;
     uint16_t* x16;                /* [n][max(H, qd, ffn)] FP16 rows for the tensor-core GEMMs */
+    uint16_t* x16b;               /* [n][ffn] FP16 gate|up output for the down-projection GEMM */
     unsigned long long* lm_keys;  /* per-CTA argmax keys of the tensor-core lm_head */
     int *d_blk;   /* [0,n) tokens, [n,2n) positions, [2n,3n) row->sequence */
     int *d_tok;
@@ -50,7 +51,7 @@ static size_t batch_bytes(const MatmulDecoderConfig* c, int n, int max_seq, int 
     t += (size_t)n * 3 * 4 + 1024;
     t += b2_attention_workspace(n, c->num_q_heads, (int)hd, split) + b2_lm_head_workspace(n, c->vocab_size);
     const size_t kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
-    t += (size_t)n * kmax * 2 + b2_gemm_argmax_keys(n, c->vocab_size) + 512;
+    t += (size_t)n * kmax * 2 + (size_t)n * F * 2 + b2_gemm_argmax_keys(n, c->vocab_size) + 768;
     return t + 4096;
 }
 
@@ -130,10 +131,11 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     {
         const size_t kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
         b->x16 = (uint16_t*)md_arena_alloc(&m->arena, n * kmax * 2);
+        b->x16b = (uint16_t*)md_arena_alloc(&m->arena, n * F * 2);
         b->lm_keys = (unsigned long long*)md_arena_alloc(&m->arena, b2_gemm_argmax_keys(n_seqs, c->vocab_size));
     }
     if (!b->k_cache || !b->v_cache || !b->hidden || !b->qkv || !b->attn || !b->act || !b->logits || !b->d_blk ||
-        !b->d_tok || !b->attn_work || !b->lm_work || !b->x16 || !b->lm_keys)
+        !b->d_tok || !b->attn_work || !b->lm_work || !b->x16 || !b->x16b || !b->lm_keys)
         rc = MATMUL_DECODER_ERR_MEMORY;
     if (!rc) rc = b2_memset(b->k_cache, 0, kv_bytes, NULL);
     if (!rc) rc = b2_memset(b->v_cache, 0, kv_bytes, NULL);
@@ -201,14 +203,14 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
     if (!rc) rc = b2_embed(b->hidden, m->emb, b->d_blk, NULL, NULL, n, H, s);
     B2KVRef kv = {b->k_cache, b->v_cache, b->seq_stride, b->layer_stride, 0, b->max_seq, b->d_blk + 2 * n,
                   b->d_blk + n, n};
-    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16, -1};
+    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16, b->x16b, -1};
     if (!rc) rc = md_enqueue_layers(m, &lb, n, &kv, s);
     if (!rc) rc = b2_event_record(b->ev[1], s);
     if (!rc && b->x16 && n >= 16 && (m->lm_wtype == B2_W_I8 || m->lm_wtype == B2_W_F16) && H % 64 == 0) {
         /* many sequences: the lm_head is a GEMM on the tensor cores with the argmax in its epilogue */
         rc = b2_rows_to_f16(b->x16, H, b->hidden, H, n, H, m->final_norm, c->rms_eps, s);
         B2GemmArgs g = {b->logits, c->vocab_size, b->x16, H, n, H, c->vocab_size, m->lm,
-                        m->lm_wtype == B2_W_I8 ? m->lm_scales : NULL, m->lm_wtype, B2_EPI_ARGMAX, b->lm_keys, b->d_tok};
+                        m->lm_wtype == B2_W_I8 ? m->lm_scales : NULL, m->lm_wtype, B2_EPI_ARGMAX, b->lm_keys, b->d_tok, NULL};
         if (!rc) rc = b2_gemm(&g, s);
     } else if (!rc) {
         rc = b2_lm_head_argmax(b->hidden, H, n, H, c->vocab_size, m->lm, m->lm_scales, m->lm_wtype, m->final_norm,

@@ -45,6 +45,7 @@ struct MatmulDecoderContext {
     long long layer_stride;
     float *hidden, *qkv, *attn, *act, *logits;
     uint16_t* x16; /* [rows_cap][max(H, qd, ffn)] FP16 rows for the prefill tensor-core GEMM */
+    uint16_t* x16b; /* [rows_cap][ffn] FP16 gate|up output for the down-projection GEMM */
     int* d_blk;    /* PARAMS_INTS ints then hidden_dim floats */
     int* d_pos;    /* [rows_cap] prefill positions */
     int* d_tok;
@@ -89,6 +90,7 @@ static size_t ctx_bytes(const MatmulDecoderConfig* c, int max_seq, int rows_cap,
     size_t t = 2 * (size_t)c->num_layers * kvd * (size_t)max_seq * 2;   /* KV cache */
     t += (size_t)rows_cap * (H + qd + 2 * kvd + qd + F) * 4 + 8 * 256;   /* activations */
     t += (size_t)rows_cap * (H > qd ? (H > F ? H : F) : (qd > F ? qd : F)) * 2 + 256; /* FP16 GEMM rows */
+    t += (size_t)rows_cap * F * 2 + 256;                                  /* FP16 gate|up output */
     t += vmax * 4 + (PARAMS_INTS + H) * 4 + (size_t)rows_cap * 4 + 1024;
     size_t aw1 = b2_attention_workspace(1, c->num_q_heads, (int)hd, split_decode);
     size_t aw2 = b2_attention_workspace(rows_cap, c->num_q_heads, (int)hd, 1);
@@ -117,7 +119,8 @@ static int ctx_alloc(MatmulDecoderContext* ctx) {
     {
         const size_t kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
         ctx->x16 = (uint16_t*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * kmax * 2);
-        if (!ctx->x16) return MATMUL_DECODER_ERR_MEMORY;
+        ctx->x16b = (uint16_t*)md_arena_alloc(&m->arena, (size_t)ctx->rows_cap * F * 2);
+        if (!ctx->x16 || !ctx->x16b) return MATMUL_DECODER_ERR_MEMORY;
     }
     ctx->logits = (float*)md_arena_alloc(&m->arena, vmax * 4);
     ctx->d_blk = (int*)md_arena_alloc(&m->arena, (PARAMS_INTS + H) * 4);
@@ -371,7 +374,7 @@ static int enqueue_token(MatmulDecoderContext* ctx, int with_head, const void* t
         rc = b2_embed(ctx->hidden, m->emb, ctx->d_blk, ctx->d_blk + 1, (const float*)(ctx->d_blk + PARAMS_INTS),
                       1, H, s);
     B2KVRef kv = kv_ref(ctx, ctx->d_blk + 4);
-    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, -1};
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1};
     if (!rc) rc = md_enqueue_layers(m, &lb, 1, &kv, s);
     if (!rc) rc = b2_event_record(ctx->ev[1], s);
     if (!rc && with_head) {
@@ -572,7 +575,7 @@ static int build_loop_graph(MatmulDecoderContext* ctx) {
     if (rc) return rc;
     int rc2 = b2_embed(ctx->hidden, m->emb, ctx->d_loop, NULL, NULL, 1, H, s);
     B2KVRef kv = kv_ref(ctx, ctx->d_loop + 1);
-    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, -1};
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1};
     if (!rc2) rc2 = md_enqueue_layers(m, &lb, 1, &kv, s);
     if (!rc2)
         rc2 = b2_lm_head_argmax(ctx->hidden, H, 1, H, m->cfg.vocab_size, m->lm, m->lm_scales, m->lm_wtype,
@@ -677,7 +680,7 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
         if (split < 1) split = 1;
         if (split > ctx->split_decode) split = ctx->split_decode;
         LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, split, ctx->x16,
-                           ctx->seq_len};
+                           ctx->x16b, ctx->seq_len};
         if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
         if (!rc) rc = md_enqueue_layers(m, &lb, rows, &kv, ctx->stream);
         if (!rc) rc = b2_event_record(ctx->ev[1], ctx->stream);

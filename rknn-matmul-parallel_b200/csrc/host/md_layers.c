@@ -37,15 +37,29 @@ static int gemm_enabled(void) {
     return v;
 }
 
+/* Whether an [M] x K -> N matmul with this weight type runs on the tensor cores. */
+static int on_tensor_cores(const LayerBuffers* b, int M, int wtype, int K, int N) {
+    return b->x16 && M >= MD_GEMM_MIN_ROWS && wtype != B2_W_F32 && K % 64 == 0 && N % 128 == 0 &&
+           gemm_enabled();
+}
+
 /* One matmul of the layer: the GEMV, or for M >= MD_GEMM_MIN_ROWS rows the
- * same operation on the tensor cores (FP16, INT8 or INT4 weights). */
-static int linear(const LayerBuffers* b, const B2GemvArgs* a, b2_stream_t s) {
-    if (b->x16 && a->M >= MD_GEMM_MIN_ROWS && a->wtype != B2_W_F32 && a->K % 64 == 0 &&
-        a->N % 128 == 0 && gemm_enabled()) {
-        int rc = b2_rows_to_f16(b->x16, a->K, a->x, a->ldx, a->M, a->K, a->norm_w, a->eps, s);
-        if (rc) return rc;
-        B2GemmArgs g = {a->y, a->ldy, b->x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype, a->epilogue,
-                        NULL, NULL};
+ * same operation on the tensor cores (FP16, INT8 or INT4 weights).  On the
+ * tensor cores the input comes from x16_in (FP16 rows of stride K, written
+ * by the previous kernel) when given, else from a->x through b2_rows_to_f16;
+ * with y16 the output is written as FP16 rows of stride a->ldy instead of
+ * a->y (the next matmul's input). */
+static int linear(const LayerBuffers* b, const B2GemvArgs* a, const uint16_t* x16_in, uint16_t* y16,
+                  b2_stream_t s) {
+    if (on_tensor_cores(b, a->M, a->wtype, a->K, a->N)) {
+        const uint16_t* x16 = x16_in;
+        if (!x16) {
+            int rc = b2_rows_to_f16(b->x16, a->K, a->x, a->ldx, a->M, a->K, a->norm_w, a->eps, s);
+            if (rc) return rc;
+            x16 = b->x16;
+        }
+        B2GemmArgs g = {y16 ? NULL : a->y, a->ldy, x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype,
+                        a->epilogue, NULL, NULL, y16};
         return b2_gemm(&g, s);
     }
     return b2_gemv(a, s);
@@ -60,7 +74,7 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         const DevLayer* L = &m->layers[l];
         B2GemvArgs a = {b->qkv, ldqkv, b->hidden, H, M, H, ldqkv, L->qkv.w, L->qkv.s, L->qkv.wtype,
                         L->in_norm, c->rms_eps, B2_EPI_STORE};
-        int rc = linear(b, &a, s);
+        int rc = linear(b, &a, NULL, NULL, s);
         if (rc) return rc;
         B2KVRef kv = *kv_proto;
         kv.layer = l;
@@ -68,22 +82,33 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         rc = b2_qk_rope_kv(b->qkv, ldqkv, M, nq, nkv, hd, qk ? L->q_norm : NULL, qk ? L->k_norm : NULL,
                            c->rms_eps, m->cos_tab, m->sin_tab, c->rope_style, &kv, s);
         if (rc) return rc;
+        /* When o_proj runs on the tensor cores, attention writes its FP16
+         * input rows directly (the rounding b2_rows_to_f16 would apply). */
+        const int o_tc = on_tensor_cores(b, M, L->o.wtype, qd, H);
+        float* attn32 = o_tc ? NULL : b->attn;
+        uint16_t* attn16 = o_tc ? b->x16 : NULL;
         if (b->prefill_base >= 0 && M >= MD_GEMM_MIN_ROWS && nq == 2 * nkv && hd == 128 && !kv.rows_seq)
-            rc = b2_attention_prefill(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->prefill_base, s);
+            rc = b2_attention_prefill(attn32, attn16, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->prefill_base, s);
+        else if (o_tc)
+            rc = b2_attention_f16(attn16, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
         else
             rc = b2_attention(b->attn, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
         if (rc) return rc;
         B2GemvArgs o = {b->hidden, H, b->attn, qd, M, qd, H, L->o.w, L->o.s, L->o.wtype, NULL, 0.f,
                         B2_EPI_ADD};
-        rc = linear(b, &o, s);
+        rc = linear(b, &o, attn16, NULL, s);
         if (rc) return rc;
+        /* gate|up writes the down projection's FP16 input when both run on
+         * the tensor cores. */
+        const int dn_tc = b->x16b && on_tensor_cores(b, M, L->gu.wtype, H, F) &&
+                          on_tensor_cores(b, M, L->down.wtype, F, H);
         B2GemvArgs gu = {b->act, F, b->hidden, H, M, H, F, L->gu.w, L->gu.s, L->gu.wtype, L->post_norm,
                          c->rms_eps, B2_EPI_SILU_PAIR};
-        rc = linear(b, &gu, s);
+        rc = linear(b, &gu, NULL, dn_tc ? b->x16b : NULL, s);
         if (rc) return rc;
         B2GemvArgs dn = {b->hidden, H, b->act, F, M, F, H, L->down.w, L->down.s, L->down.wtype, NULL, 0.f,
                          B2_EPI_ADD};
-        rc = linear(b, &dn, s);
+        rc = linear(b, &dn, dn_tc ? b->x16b : NULL, NULL, s);
         if (rc) return rc;
     }
     return 0;

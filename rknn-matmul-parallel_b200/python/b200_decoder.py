@@ -51,7 +51,7 @@ class B2GemvArgs(ctypes.Structure):
 class B2GemmArgs(ctypes.Structure):
     _fields_ = [("y", c_vp), ("ldy", c_int), ("x16", c_vp), ("ldx", c_int), ("M", c_int),
                 ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
-                ("epilogue", c_int), ("keys", c_vp), ("tokens", c_vp)]
+                ("epilogue", c_int), ("keys", c_vp), ("tokens", c_vp), ("y16", c_vp)]
 
 
 class B2KVRef(ctypes.Structure):
@@ -127,7 +127,7 @@ SIGNATURES = {
     "b2_graph_destroy": (c_int, [c_vp]),
     "b2_gemv": (c_int, [c_vp, c_vp]),
     "b2_gemm": (c_int, [c_vp, c_vp]),
-    "b2_attention_prefill": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp]),
+    "b2_attention_prefill": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp]),
     "b2_gemm_argmax_keys": (ctypes.c_size_t, [c_int, c_int]),
     "b2_rows_to_f16": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_int, c_vp, c_float, c_vp]),
     "b2_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
@@ -135,6 +135,7 @@ SIGNATURES = {
                               c_vp, c_vp, c_int, c_vp, c_vp]),
     "b2_attention_workspace": (c_size, [c_int, c_int, c_int, c_int]),
     "b2_attention": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp]),
+    "b2_attention_f16": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp]),
     "b2_lm_head_workspace": (c_size, [c_int, c_int]),
     "b2_loop_advance": (c_int, [c_vp, c_vp, c_int, c_vp]),
     "b2_lm_head_noalloc_max_keys": (c_size, []),

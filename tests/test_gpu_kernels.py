@@ -400,8 +400,11 @@ def test_attention_prefill_flash_matches_oracle(M, base):
     kc_d, vc_d, q_d = dev(kc), dev(vc), dev(q)
     kv = kv_ref(kc_d, vc_d, 0, max_seq, dev(pos))
     out_f = torch.empty((M, nq * hd), dtype=torch.float32, device=DEV)
-    bd.check(bd.capi().b2_attention_prefill(out_f.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
+    bd.check(bd.capi().b2_attention_prefill(out_f.data_ptr(), None, q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
                                             ctypes.byref(kv), base, stream()), "attention_prefill")
+    out_h = torch.empty((M, nq * hd), dtype=torch.float16, device=DEV)
+    bd.check(bd.capi().b2_attention_prefill(None, out_h.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
+                                            ctypes.byref(kv), base, stream()), "attention_prefill f16")
     work = torch.empty(bd.capi().b2_attention_workspace(M, nq, hd, 0), dtype=torch.uint8, device=DEV)
     out_s = torch.empty((M, nq * hd), dtype=torch.float32, device=DEV)
     bd.check(bd.capi().b2_attention(out_s.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd, ctypes.byref(kv),
@@ -409,6 +412,7 @@ def test_attention_prefill_flash_matches_oracle(M, base):
     torch.cuda.synchronize()
     flash, split = out_f.cpu().numpy(), out_s.cpu().numpy()
     assert_close(flash, split, rtol=2e-2, atol=5e-3)
+    np.testing.assert_array_equal(out_h.cpu().numpy(), flash.astype(np.float16))  # same values, rounded
     for m in sorted({0, M // 3, M - 1}):
         L = base + m + 1
         exp = ref.attention(q[m], kc[:, :L].transpose(1, 0, 2).astype(np.float32),
@@ -418,8 +422,8 @@ def test_attention_prefill_flash_matches_oracle(M, base):
 
 def test_attention_prefill_rejects_unsupported():
     kv = bd.B2KVRef(16, 16, 0, 0, 0, 64, None, 16, 1)
-    assert bd.capi().b2_attention_prefill(16, 16, 2048, 8, 24, 8, 128, ctypes.byref(kv), 0, None) == -1  # G = 3
-    assert bd.capi().b2_attention_prefill(16, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 60, None) == -1  # past max_seq
+    assert bd.capi().b2_attention_prefill(16, None, 16, 2048, 8, 24, 8, 128, ctypes.byref(kv), 0, None) == -1  # G = 3
+    assert bd.capi().b2_attention_prefill(16, None, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 60, None) == -1  # past max_seq
 
 
 def lm_reference(x, norm_w, table, scales, wtype):
