@@ -138,6 +138,9 @@ typedef struct {
     int* tokens;
     uint16_t* y16; /* STORE / SILU_PAIR: when not NULL, the output as FP16 rows
                       (stride ldy) instead of y, e.g. the next GEMM's x16 */
+    int split_k;   /* CTAs (a thread-block cluster) sharing one output tile's K
+                      range: 0 = chosen from the grid and SM count, else 1, 2,
+                      4 or 8 (<= K / 64) */
 } B2GemmArgs;
 size_t b2_gemm_argmax_keys(int M, int N);
 int b2_gemm(const B2GemmArgs* a, b2_stream_t s);

@@ -13,11 +13,12 @@
 //   warp 1       allocates the tensor-memory accumulator and one thread issues
 //                tcgen05.mma (M=128, N=BN, K=16, FP16 x FP16 -> FP32),
 //                committing each stage back to the loader;
-//   warps 2-5    for INT8 / INT4 weights, widen each stage's raw weight tile
+//   warps 2-9    for INT8 / INT4 weights, widen each stage's raw weight tile
 //                exactly to FP16 in the swizzled layout the MMA reads (the
 //                integer in the mantissa of 1024 and one half2 subtraction);
 //                at the end, read the accumulator with tcgen05.ld (warp w owns
-//                TMEM lanes 32*(w%4)..+31) and apply the epilogue.
+//                TMEM lanes 32*(w%4)..+31; warps 2-5 and 6-9 take alternate
+//                16-column chunks) and apply the epilogue.
 //
 // The weight tile is the MMA's A operand (output columns are TMEM lanes) and
 // the activation tile its B operand (token rows are TMEM columns), so one
@@ -30,6 +31,7 @@
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is looked up at run time
 
 #include <mutex>
+#include <stdlib.h>
 
 #include "b2_common.cuh"
 
@@ -37,7 +39,8 @@ namespace {
 
 constexpr int kBM = 128;     // weight rows per tile (MMA M)
 constexpr int kBK = 64;      // k per stage: 64 FP16 = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer warp, MMA warp, 8 converter / epilogue warps
+constexpr int kWork = kThreads - 64;
 constexpr int kMaxStages = 8;
 constexpr long long kWaitLimit = 1ll << 22;
 
@@ -78,6 +81,7 @@ struct Bars {
     uint64_t done;
     uint32_t tmem;
     int failed;
+    int peer_failed[8];  // split-K: failure flag of each cluster rank, pushed by that rank
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -165,27 +169,69 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// Eight consecutive weights (k = 8c .. 8c+7 of a row) widened exactly to FP16.
-template <int WT>
-__device__ __forceinline__ uint4 widen8(const unsigned char* raw) {
+// Eight consecutive weights widened exactly to FP16 (the integer in the
+// mantissa of 1024 and one half2 subtraction of 1024 + bias).
+// INT8: two words, byte i of the pair is k = i.
+__device__ __forceinline__ uint4 widen8_i8(uint32_t w0, uint32_t w1) {
+    const uint32_t bias = 0x64806480u;  // half2(1152): 1024 + 128
+    const uint32_t a = w0 ^ 0x80808080u, b = w1 ^ 0x80808080u;
     uint4 h;
-    if constexpr (WT == B2_W_I8) {
-        const uint2 w = *reinterpret_cast<const uint2*>(raw);
-        const uint32_t bias = 0x64806480u;  // half2(1152): 1024 + 128
-        const uint32_t a = w.x ^ 0x80808080u, b = w.y ^ 0x80808080u;
-        h.x = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4140), bias);
-        h.y = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4342), bias);
-        h.z = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4140), bias);
-        h.w = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4342), bias);
-    } else {  // INT4: nibble i of the word is k = 8c + i (even k in the low nibble of its byte)
-        const uint32_t u = *reinterpret_cast<const uint32_t*>(raw) ^ 0x88888888u;
-        const uint32_t bias = 0x64086408u;  // half2(1032): 1024 + 8
-        h.x = hsub2_u32((u & 0x0000000Fu) | ((u << 12) & 0x000F0000u) | 0x64006400u, bias);
-        h.y = hsub2_u32(((u >> 8) & 0x0000000Fu) | ((u << 4) & 0x000F0000u) | 0x64006400u, bias);
-        h.z = hsub2_u32(((u >> 16) & 0x0000000Fu) | ((u >> 4) & 0x000F0000u) | 0x64006400u, bias);
-        h.w = hsub2_u32(((u >> 24) & 0x0000000Fu) | ((u >> 12) & 0x000F0000u) | 0x64006400u, bias);
-    }
+    h.x = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4140), bias);
+    h.y = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4342), bias);
+    h.z = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4140), bias);
+    h.w = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4342), bias);
     return h;
+}
+// INT4: one word, nibble i is k = i (even k in the low nibble of its byte).
+__device__ __forceinline__ uint4 widen8_i4(uint32_t w) {
+    const uint32_t u = w ^ 0x88888888u;
+    const uint32_t bias = 0x64086408u;  // half2(1032): 1024 + 8
+    uint4 h;
+    h.x = hsub2_u32((u & 0x0000000Fu) | ((u << 12) & 0x000F0000u) | 0x64006400u, bias);
+    h.y = hsub2_u32(((u >> 8) & 0x0000000Fu) | ((u << 4) & 0x000F0000u) | 0x64006400u, bias);
+    h.z = hsub2_u32(((u >> 16) & 0x0000000Fu) | ((u >> 4) & 0x000F0000u) | 0x64006400u, bias);
+    h.w = hsub2_u32(((u >> 24) & 0x0000000Fu) | ((u >> 12) & 0x000F0000u) | 0x64006400u, bias);
+    return h;
+}
+
+// ── thread-block cluster helpers (split-K partial sums through distributed shared memory) ──
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+// Stores into another CTA's shared memory do not stall the issuing thread;
+// the cluster barrier's release / acquire makes them visible.
+__device__ __forceinline__ void st_dsmem4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void st_dsmem_s32(uint32_t addr, int v) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// Split-K receive buffer of the CTA that finishes a slice of W accumulator
+// columns: slot r (the sending rank) holds its partial sums of the slice as
+// groups of 4 columns, [r][lc / 4][128 rows][4] FP32, so one warp's 16-byte
+// accesses to a column group are 512 contiguous bytes.  lc is the column
+// within the slice (a multiple of 4 here).
+__device__ __forceinline__ uint32_t part_off(int r, int W, int lc, int li) {
+    return (uint32_t)((((r * W + lc) >> 2) * kBM + li) * 16);
+}
+
+// silu(g) * u with the sigmoid as 1 / (1 + e^-g) from the fast exponential
+// and divide (relative error ~1e-6, inside the FP32 parity tolerance); the
+// exponent is capped where e^-g would leave the divide's range.
+__device__ __forceinline__ float silu_mul(float gv, float uv) {
+    return gv * __fdividef(1.0f, 1.0f + __expf(fminf(-gv, 80.0f))) * uv;
 }
 
 template <int BN, int MODE, int WT>
@@ -193,21 +239,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const GemmParams g) {
     using Lay = Layout<BN, MODE, WT>;
     constexpr bool kConvert = WT != B2_W_F16;
+    static_assert(kBM * Lay::kCols * 4 + 4 * BN * 8 <= Lay::kStages * Lay::kStage, "epilogue scratch exceeds the ring");
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     Bars* b = reinterpret_cast<Bars*>(smem + Lay::kStages * Lay::kStage);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BN;
-    // split-K (ADD epilogue only): this CTA sums k stages [kt0, kt0 + KT)
+    // split-K: the gridDim.z CTAs of a tile form one cluster; this CTA sums k
+    // stages [kt0, kt0 + KT) and the cluster reduces the partial sums.
+    const int S = (int)gridDim.z;
     const int KT_all = g.K / kBK;
-    const int kt0 = (int)((long long)KT_all * blockIdx.z / gridDim.z);
-    const int KT = (int)((long long)KT_all * (blockIdx.z + 1) / gridDim.z) - kt0;
+    const int kt0 = (int)((long long)KT_all * blockIdx.z / S);
+    const int KT = (int)((long long)KT_all * (blockIdx.z + 1) / S) - kt0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Lay::kStages; s++) {
             mbar_init(&b->full[s], 1);
-            mbar_init(&b->conv[s], 4);
+            mbar_init(&b->conv[s], kWork / 32);
             mbar_init(&b->empty[s], 1);
         }
         mbar_init(&b->done, 1);
@@ -226,16 +275,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = b->tmem;
-    // The activation rows come from the previous kernel of the stream.
-    b2::pdl_wait();
+    bool ok = true;
+    // Let the next kernel of the stream start its own prologue on the SMs
+    // this grid leaves free; it waits for this grid's completion before it
+    // reads anything this grid writes.
+    b2::pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
             constexpr uint32_t kTx = Lay::kB + (kConvert ? Lay::kRaw : Lay::kA);
             constexpr int kWTile = kConvert ? kBM * raw_row_bytes<WT>() : kBM * 128;
-            for (int kt = 0; kt < KT; kt++) {
+            auto load_w = [&](int kt) {
                 const int s = kt % Lay::kStages;
-                if (kt >= Lay::kStages && !mbar_wait(&b->empty[s], (uint32_t)((kt / Lay::kStages - 1) & 1), b)) break;
                 unsigned char* st = smem + s * Lay::kStage;
                 unsigned char* wdst = kConvert ? st + Lay::kA + Lay::kB : st;
                 // x coordinate of the weight map: elements for FP16, bytes for INT8/INT4
@@ -243,7 +294,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(&b->full[s], kTx);
                 tma_load_2d(wdst, &tw, wx, kBM * blockIdx.x, &b->full[s]);
                 if (MODE == MODE_PAIR) tma_load_2d(wdst + kWTile, &tw, wx, g.N + kBM * blockIdx.x, &b->full[s]);
-                tma_load_2d(st + Lay::kA, &tx, (kt0 + kt) * kBK, m0, &b->full[s]);
+            };
+            auto load_x = [&](int kt) {
+                const int s = kt % Lay::kStages;
+                tma_load_2d(smem + s * Lay::kStage + Lay::kA, &tx, (kt0 + kt) * kBK, m0, &b->full[s]);
+            };
+            // The weights do not depend on earlier kernels of the stream: the
+            // first ring's worth is requested before waiting for them.
+            const int pre = KT < Lay::kStages ? KT : Lay::kStages;
+            for (int kt = 0; kt < pre; kt++) load_w(kt);
+            // The activation rows come from the previous kernel of the stream.
+            b2::pdl_wait();
+            for (int kt = 0; kt < pre; kt++) load_x(kt);
+            for (int kt = pre; kt < KT; kt++) {
+                const int s = kt % Lay::kStages;
+                if (!mbar_wait(&b->empty[s], (uint32_t)((kt / Lay::kStages - 1) & 1), b)) break;
+                load_w(kt);
+                load_x(kt);
             }
         }
     } else if (warp == 1) {
@@ -266,22 +333,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             umma_commit(&b->done);
         }
-    } else {  // warps 2..5
-        const int et = threadIdx.x - 64;  // 0..127
+    } else {  // warps 2..9
+        const int et = threadIdx.x - 64;  // 0..kWork-1
         if constexpr (kConvert) {
-            // raw [rows][raw_row_bytes] -> FP16 [rows][128 B] with chunk c of row r at (c ^ (r % 8)) * 16
+            // raw [rows][raw_row_bytes] -> FP16 [rows][128 B] with 16-byte chunk c of row r at (c ^ (r % 8)) * 16.
+            // Each thread widens whole 16-byte raw chunks (16 INT8 or 32 INT4 weights); all of a stage's
+            // loads are issued before its stores.
+            constexpr int kRowChunks = raw_row_bytes<WT>() / 16;               // raw chunks per row
+            constexpr int kOut = 8 / kRowChunks;                               // FP16 chunks per raw chunk
+            constexpr int kPer = Lay::kATiles * kBM * kRowChunks / kWork;      // raw chunks per thread
+            static_assert(kPer * kWork == Lay::kATiles * kBM * kRowChunks, "converter jobs must divide evenly");
             for (int kt = 0; kt < KT; kt++) {
                 const int s = kt % Lay::kStages;
                 if (!mbar_wait(&b->full[s], (uint32_t)((kt / Lay::kStages) & 1), b)) break;
                 unsigned char* st = smem + s * Lay::kStage;
-                const unsigned char* raw = st + Lay::kA + Lay::kB;
-#pragma unroll 4
-                for (int job = et; job < Lay::kATiles * kBM * 8; job += 128) {
-                    const int tile = job / (kBM * 8), r = (job >> 3) % kBM, c = job & 7;
-                    const uint4 h = widen8<WT>(raw + (size_t)(tile * kBM + r) * raw_row_bytes<WT>() +
-                                               c * (raw_row_bytes<WT>() / 8));
-                    *reinterpret_cast<uint4*>(st + tile * kBM * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
-                                              ((c ^ (r & 7)) << 4)) = h;
+                const uint4* raw = reinterpret_cast<const uint4*>(st + Lay::kA + Lay::kB);
+                uint4 rv[kPer];
+#pragma unroll
+                for (int i = 0; i < kPer; i++) rv[i] = raw[et + kWork * i];
+#pragma unroll
+                for (int i = 0; i < kPer; i++) {
+                    const int job = et + kWork * i;
+                    const int R = job / kRowChunks, h = job % kRowChunks;  // row of the stage, raw chunk
+                    const int tile = R / kBM, r = R % kBM;
+                    unsigned char* row = st + tile * kBM * 128 + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                    for (int o = 0; o < kOut; o++) {
+                        const int c = h * kOut + o;
+                        const uint32_t* w = &rv[i].x;
+                        const uint4 hv = WT == B2_W_I8 ? widen8_i8(w[2 * o], w[2 * o + 1]) : widen8_i4(w[o]);
+                        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = hv;
+                    }
                 }
                 // the tensor cores read shared memory through the async proxy
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -289,25 +371,88 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&b->conv[s]);
             }
         }
-        const int quad = warp & 3;  // TMEM lanes this warp may read
-        const bool ok = mbar_wait(&b->done, 0, b);
+        ok = mbar_wait(&b->done, 0, b);
         tc_fence_after();
-        const int n = kBM * blockIdx.x + 32 * quad + lane;
+    }
+    // Split-K reduction.  The token columns [0, BN) are cut into S slices;
+    // rank j finishes slice j (for SILU_PAIR the gate and the up columns of
+    // those tokens).  Once every CTA of the cluster has finished its k loop
+    // (its ring is idle), each pushes the partial sums of slice j into rank
+    // j's ring, then the owners add the S partials from their own memory.
+    constexpr int kSliceCols = MODE == MODE_PAIR ? 2 : 1;  // accumulator columns per token
+    const int W = kSliceCols * BN / S;                      // accumulator columns per slice
+    if (S > 1) {
+        cluster_sync();
+        if (warp >= 2) {
+            const int quad = warp & 3, li = 32 * quad + lane, half = (warp - 2) >> 2;
+            const int me = (int)cluster_rank();
+            const bool bad = !ok || *(volatile int*)&b->failed;
+            if (threadIdx.x == 64)
+                for (int j = 0; j < S; j++) st_dsmem_s32(dsmem_addr(smem_u32(&b->peer_failed[me]), j), bad ? 1 : 0);
+            if (!bad) {
+                // chunks in an order rotated by rank, so the ranks start on different owners
+                constexpr int kChunks = Lay::kCols / 16;
+#pragma unroll 1
+                for (int i = half; i < kChunks; i += 2) {
+                    const int c0 = 16 * ((i + me * kChunks / S) % kChunks);
+                    uint32_t v[16];
+                    tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int col = c0 + 4 * q, tok = col % BN, j = tok / (BN / S);
+                        const int lc = (col >= BN ? W / 2 : 0) + tok - j * (BN / S);
+                        st_dsmem4(dsmem_addr(smem_u32(smem + part_off(me, W, lc, li)), j), v[4 * q], v[4 * q + 1],
+                                  v[4 * q + 2], v[4 * q + 3]);
+                    }
+                }
+            }
+        }
+        cluster_sync();
+    }
+    if (warp >= 2) {
+        const int et = threadIdx.x - 64;
+        const int quad = warp & 3, li = 32 * quad + lane, half = (warp - 2) >> 2;
+        const int n = kBM * blockIdx.x + li;
+        // This CTA's token columns: all of them, or with split-K its slice.
+        const int rank = S > 1 ? (int)cluster_rank() : 0;
+        const int cb = rank * BN / S, ce = (rank + 1) * BN / S;
+        if (S > 1)
+            for (int r = 0; r < S; r++) ok = ok && *(volatile int*)&b->peer_failed[r] == 0;
+        // v[j] = accumulator column col + j (j < cnt) of row li; with split-K
+        // col is relative to the slice (lc) and the S partials are summed.
+        auto acc16 = [&](int col, int cnt, uint32_t (&v)[16]) {
+            if (S == 1) {
+                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + col, v);
+                return;
+            }
+            float f[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) f[j] = 0.f;
+            for (int r = 0; r < S; r++) {
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    if (4 * q >= cnt) break;
+                    const float4 p = *reinterpret_cast<const float4*>(smem + part_off(r, W, col + 4 * q, li));
+                    f[4 * q] += p.x;
+                    f[4 * q + 1] += p.y;
+                    f[4 * q + 2] += p.z;
+                    f[4 * q + 3] += p.w;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = __float_as_uint(f[j]);
+        };
+        b2::pdl_wait();  // y may be read (residual) and is written below
         if (MODE == MODE_ROWS) {
             const float sc = g.scales ? g.scales[n] : 1.f;
-            const bool split = gridDim.z > 1;  // partial sums: add atomically into y
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN && ok; c0 += 16) {
+            for (int c0 = cb + 16 * half; c0 < ce && ok; c0 += 32) {
                 uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
-                const int jn = min(16, g.M - (m0 + c0));
+                acc16(S > 1 ? c0 - cb : c0, min(16, ce - c0), v);
+                const int jn = min(min(16, ce - c0), g.M - (m0 + c0));
                 if (jn <= 0) break;
                 float* yp = g.y + (size_t)(m0 + c0) * g.ldy + n;
-                if (split) {
-#pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        if (j < jn) atomicAdd(yp + (size_t)j * g.ldy, __uint_as_float(v[j]) * sc);
-                } else if (g.epilogue == B2_EPI_ADD) {
+                if (g.epilogue == B2_EPI_ADD) {
                     float old[16];  // all loads first, then the stores
 #pragma unroll
                     for (int j = 0; j < 16; j++) old[j] = j < jn ? yp[(size_t)j * g.ldy] : 0.f;
@@ -329,32 +474,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             // lane = channel n: gate sum in columns [0, BN), up sum in [BN, 2 BN)
             const float sg = g.scales ? g.scales[n] : 1.f, su = g.scales ? g.scales[g.N + n] : 1.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN && ok; c0 += 16) {
+            for (int c0 = cb + 16 * half; c0 < ce && ok; c0 += 32) {
                 uint32_t vg[16], vu[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, vg);
-                tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + BN + c0, vu);
-                const int jn = min(16, g.M - (m0 + c0));
+                acc16(S > 1 ? c0 - cb : c0, min(16, ce - c0), vg);
+                acc16(S > 1 ? W / 2 + c0 - cb : BN + c0, min(16, ce - c0), vu);
+                const int jn = min(min(16, ce - c0), g.M - (m0 + c0));
                 if (jn <= 0) break;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     if (j >= jn) break;
-                    const float gv = __uint_as_float(vg[j]) * sg, uv = __uint_as_float(vu[j]) * su;
-                    const float sig = 1.0f / (1.0f + expf(-gv));
+                    const float h = silu_mul(__uint_as_float(vg[j]) * sg, __uint_as_float(vu[j]) * su);
                     const size_t o = (size_t)(m0 + c0 + j) * g.ldy + n;
-                    if (g.y16) g.y16[o] = __float2half_rn((gv * sig) * uv);  // the down GEMM's FP16 input
-                    else g.y[o] = (gv * sig) * uv;
+                    if (g.y16) g.y16[o] = __float2half_rn(h);  // the down GEMM's FP16 input
+                    else g.y[o] = h;
                 }
             }
         } else {  // ARGMAX over this CTA's 128 vocab rows, per token
-            unsigned long long* kq = reinterpret_cast<unsigned long long*>(smem);  // [4][BN]; the ring is idle
+            // [4][BN] keys after the partial-sum area; the ring is idle
+            unsigned long long* kq = reinterpret_cast<unsigned long long*>(smem + kBM * Lay::kCols * 4);
             const bool live = n < g.N;
             const float sc = live ? (g.scales ? g.scales[n] : 1.f) : 0.f;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            for (int c0 = cb + 16 * half; c0 < ce; c0 += 32) {
                 uint32_t v[16];
-                if (ok) tmem_ld16(tmem + ((uint32_t)(32 * quad) << 16) + c0, v);
+                if (ok) acc16(S > 1 ? c0 - cb : c0, min(16, ce - c0), v);
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
+                    if (c0 + j >= ce) break;  // uniform across the warp
                     const int m = m0 + c0 + j;
                     const float logit = ok ? __uint_as_float(v[j]) * sc : 0.f;
                     if (g.y && live && m < g.M) g.y[(size_t)m * g.ldy + n] = logit;
@@ -363,8 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) kq[quad * BN + c0 + j] = key;
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int j = et; j < BN; j += 128) {
+            asm volatile("bar.sync 1, %0;" ::"n"(kWork) : "memory");
+            for (int j = cb + et; j < ce; j += kWork) {
                 unsigned long long key = kq[j];
 #pragma unroll
                 for (int q = 1; q < 4; q++) key = kq[q * BN + j] > key ? kq[q * BN + j] : key;
@@ -372,7 +518,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    b2::pdl_trigger();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -386,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256) argmax_parts_kernel(const unsigned long long* __restrict__ keys, int nparts,
                                                            int* __restrict__ tokens) {
     __shared__ unsigned long long sm[8];
+    b2::pdl_trigger();
     b2::pdl_wait();
     unsigned long long k = 0ull;
     for (int i = threadIdx.x; i < nparts; i += 256) {
@@ -399,7 +545,6 @@ __global__ void __launch_bounds__(256) argmax_parts_kernel(const unsigned long l
         for (int w = 0; w < 8; w++) k = sm[w] > k ? sm[w] : k;
         tokens[blockIdx.x] = (int)b2::key_index(k);
     }
-    b2::pdl_trigger();
 }
 
 // ── b2_rows_to_f16: one CTA per row ──
@@ -407,6 +552,7 @@ __global__ void __launch_bounds__(256) rows_to_f16_kernel(uint16_t* __restrict__
                                                          const float* __restrict__ x, int ldx, int K,
                                                          const float* __restrict__ norm_w, float eps) {
     __shared__ float red[8];
+    b2::pdl_trigger();
     b2::pdl_wait();
     const float* xr = x + (size_t)blockIdx.x * ldx;
     __half* yr = reinterpret_cast<__half*>(y16) + (size_t)blockIdx.x * ldy;
@@ -428,7 +574,6 @@ __global__ void __launch_bounds__(256) rows_to_f16_kernel(uint16_t* __restrict__
         if (norm_w) v = (v * rms) * norm_w[k];
         yr[k] = __float2half_rn(v);
     }
-    b2::pdl_trigger();
 }
 
 // ── host side ──
@@ -468,6 +613,17 @@ int make_map(CUtensorMap* m, const void* base, bool f16, uint64_t inner, uint64_
     return 0;
 }
 
+// B2_GEMM_SPLIT=1|2|4|8 fixes the split-K cluster size of every call that
+// leaves it to the library (split_k == 0); unset or 0 keeps the automatic choice.
+int split_override() {
+    static const int v = [] {
+        const char* e = getenv("B2_GEMM_SPLIT");
+        const int x = e ? atoi(e) : 0;
+        return (x == 1 || x == 2 || x == 4 || x == 8) ? x : 0;
+    }();
+    return v;
+}
+
 template <int BN, int MODE, int WT>
 int launch(const B2GemmArgs* a, cudaStream_t s, int sms) {
     using Lay = Layout<BN, MODE, WT>;
@@ -488,13 +644,55 @@ int launch(const B2GemmArgs* a, cudaStream_t s, int sms) {
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm smem attr: %s", cudaGetErrorString(e));
     GemmParams g{a->y, a->ldy, a->M, a->K, a->N, a->scales, a->epilogue, a->keys,
                  reinterpret_cast<__half*>(a->y16)};
-    const int gx = (a->N + kBM - 1) / kBM, gy = (a->M + BN - 1) / BN;
-    // A residual-add GEMM whose grid leaves SMs idle splits K over more CTAs
-    // (each adds its partial sum into y; at least 4 k stages per split).
-    int split = 1;
-    if (MODE == MODE_ROWS && a->epilogue == B2_EPI_ADD)
-        while (gx * gy * split * 2 <= sms && (a->K / kBK) / (split * 2) >= 4) split *= 2;
-    e = b2::launch_pdl(fn, dim3(gx, gy, split), dim3(kThreads), smem, s, tw, tx, g);
+    const int gx = (a->N + kBM - 1) / kBM, gy = (a->M + BN - 1) / BN, KT = a->K / kBK;
+    // Split-K over a cluster of S CTAs per tile when the tiles alone leave
+    // SMs idle (each CTA keeps at least two k stages); the cluster reduces
+    // the partial sums, so every epilogue sees whole sums.
+    int S = a->split_k;
+    if (S <= 0) S = split_override();
+    if (S <= 0) {
+        S = 1;
+        while (S < 8 && gx * gy * S * 2 <= sms && KT / (S * 2) >= 2) S *= 2;
+    }
+    while (S > KT) S /= 2;
+    if (S > 1) {  // a cluster of S full-shared-memory CTAs must fit the GPU
+        static int fits[4] = {-1, -1, -1, -1};  // S = 2, 4, 8 (index log2 S)
+        int& f = fits[S == 2 ? 1 : S == 4 ? 2 : 3];
+        if (f < 0) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(gx, gy, S);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 1;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = S;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            f = cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n > 0;
+            cudaGetLastError();
+        }
+        if (!f) S = 1;
+    }
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(gx, gy, S);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = 1;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = S;
+        cfg.attrs = at;
+        cfg.numAttrs = S > 1 ? 2 : 1;
+        e = cudaLaunchKernelEx(&cfg, fn, tw, tx, g);
+    }
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_gemm launch: %s", cudaGetErrorString(e));
     if (MODE == MODE_ARGMAX) {
         e = b2::launch_pdl(argmax_parts_kernel, dim3(a->M), dim3(256), 0, s, (const unsigned long long*)a->keys, gx,
@@ -533,11 +731,13 @@ extern "C" int b2_gemm(const B2GemmArgs* a, b2_stream_t stream) {
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_gemm: missing output for epilogue %d", epi);
     if ((a->wtype != B2_W_F16 && a->wtype != B2_W_I8 && a->wtype != B2_W_I4) ||
         (a->wtype != B2_W_F16 && !a->scales) || a->K % kBK || (!argmax && a->N % kBM) || a->ldx % 8 ||
-        a->ldx < a->K || ((a->y || a->y16) && a->ldy < a->N) || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
+        a->ldx < a->K || ((a->y || a->y16) && a->ldy < a->N) ||
+        (a->split_k != 0 && a->split_k != 1 && a->split_k != 2 && a->split_k != 4 && a->split_k != 8) ||
+        a->split_k > a->K / kBK || (reinterpret_cast<uintptr_t>(a->x16) & 15) ||
         (reinterpret_cast<uintptr_t>(a->w) & 15))
         return b2_set_error(B2_ERR_INVALID_ARG,
                             "b2_gemm: needs F16/I8/I4 weights (scales for I8/I4), K %% 64 == 0, N %% 128 == 0, "
-                            "ldx %% 8 == 0, aligned operands");
+                            "ldx %% 8 == 0, aligned operands, split_k in {0, 1, 2, 4, 8} and <= K / 64");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

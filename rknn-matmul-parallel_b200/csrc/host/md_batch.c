@@ -210,7 +210,7 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
         /* many sequences: the lm_head is a GEMM on the tensor cores with the argmax in its epilogue */
         rc = b2_rows_to_f16(b->x16, H, b->hidden, H, n, H, m->final_norm, c->rms_eps, s);
         B2GemmArgs g = {b->logits, c->vocab_size, b->x16, H, n, H, c->vocab_size, m->lm,
-                        m->lm_wtype == B2_W_I8 ? m->lm_scales : NULL, m->lm_wtype, B2_EPI_ARGMAX, b->lm_keys, b->d_tok, NULL};
+                        m->lm_wtype == B2_W_I8 ? m->lm_scales : NULL, m->lm_wtype, B2_EPI_ARGMAX, b->lm_keys, b->d_tok, NULL, 0};
         if (!rc) rc = b2_gemm(&g, s);
     } else if (!rc) {
         rc = b2_lm_head_argmax(b->hidden, H, n, H, c->vocab_size, m->lm, m->lm_scales, m->lm_wtype, m->final_norm,

@@ -59,7 +59,7 @@ static int linear(const LayerBuffers* b, const B2GemvArgs* a, const uint16_t* x1
             x16 = b->x16;
         }
         B2GemmArgs g = {y16 ? NULL : a->y, a->ldy, x16, a->K, a->M, a->K, a->N, a->w, a->scales, a->wtype,
-                        a->epilogue, NULL, NULL, y16};
+                        a->epilogue, NULL, NULL, y16, 0};
         return b2_gemm(&g, s);
     }
     return b2_gemv(a, s);

@@ -51,7 +51,8 @@ class B2GemvArgs(ctypes.Structure):
 class B2GemmArgs(ctypes.Structure):
     _fields_ = [("y", c_vp), ("ldy", c_int), ("x16", c_vp), ("ldx", c_int), ("M", c_int),
                 ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
-                ("epilogue", c_int), ("keys", c_vp), ("tokens", c_vp), ("y16", c_vp)]
+                ("epilogue", c_int), ("keys", c_vp), ("tokens", c_vp), ("y16", c_vp),
+                ("split_k", c_int)]
 
 
 class B2KVRef(ctypes.Structure):

@@ -300,6 +300,60 @@ def test_gemm_tensor_cores_lm_head_argmax(V):
         assert toks[m] == int(np.argmax(logits[m]))
 
 
+@pytest.mark.parametrize("wtype", [bd.W_F16, bd.W_I8, bd.W_I4])
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("M", [40, 130])
+def test_gemm_split_k_cluster_all_epilogues(wtype, split, M):
+    """Split-K over a thread-block cluster (each CTA sums K / split, the
+    partial sums are reduced through distributed shared memory and each CTA
+    finishes 1/split of the token columns) against the oracle for every
+    epilogue: STORE (FP32 and FP16 rows), ADD, SILU_PAIR (FP16 rows) and
+    ARGMAX.  M = 40 leaves whole token slices empty at split 8."""
+    K, N = 1024, 1024
+    rng = np.random.default_rng(7000 + 100 * wtype + 10 * split + M)
+    wf, s, rwt = make_weight(rng, K, N, wtype)
+    wu, su, _ = make_weight(rng, K, N, wtype)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    norm_w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    xn = np.stack([ref.rms_norm(r, norm_w) for r in x])
+    exp = ref.gemm(xn, wf, s, wtype=rwt, n=N)
+    x16 = rows_f16(dev(x), M, K, norm_w)
+    w_d = dev(device_rows(wf, wtype, N))
+    s_d = dev(s).data_ptr() if s is not None else None
+
+    def run(y, epi, w=w_d.data_ptr(), sc=s_d, y16=None, keys=None, toks=None):
+        a = bd.B2GemmArgs(y, N, x16.data_ptr(), K, M, K, N, w, sc, wtype, epi, keys, toks, y16, split)
+        bd.check(bd.capi().b2_gemm(ctypes.byref(a), stream()), f"b2_gemm split {split}")
+        torch.cuda.synchronize()
+
+    y_d = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    run(y_d.data_ptr(), bd.EPI_STORE)
+    assert_close(y_d.cpu().numpy(), exp)
+    h_d = torch.zeros((M, N), dtype=torch.float16, device=DEV)
+    run(None, bd.EPI_STORE, y16=h_d.data_ptr())
+    np.testing.assert_array_equal(h_d.cpu().numpy(), y_d.cpu().numpy().astype(np.float16))
+    y0 = rng.standard_normal((M, N), dtype=np.float32)
+    y_d = dev(y0.copy())
+    run(y_d.data_ptr(), bd.EPI_ADD)
+    assert_close(y_d.cpu().numpy(), y0 + exp)
+    # gate|up pair: gate rows then up rows, SiLU(gate) * up as FP16 rows
+    up = ref.gemm(xn, wu, su, wtype=rwt, n=N)
+    pair_exp = np.stack([ref.silu_mul(exp[i], up[i]) for i in range(M)])
+    rows = dev(np.concatenate([device_rows(wf, wtype, N), device_rows(wu, wtype, N)]))
+    sc2 = dev(np.concatenate([s, su])).data_ptr() if s is not None else None
+    h_d = torch.zeros((M, N), dtype=torch.float16, device=DEV)
+    run(None, bd.EPI_SILU_PAIR, w=rows.data_ptr(), sc=sc2, y16=h_d.data_ptr())
+    assert_close(h_d.float().cpu().numpy(), pair_exp, rtol=4e-3, atol=4e-3)
+    # argmax of the kernel's own logits, first index on ties
+    logits_d = torch.zeros((M, N), dtype=torch.float32, device=DEV)
+    tok_d = torch.full((M,), -1, dtype=torch.int32, device=DEV)
+    keys = torch.empty(bd.capi().b2_gemm_argmax_keys(M, N), dtype=torch.uint8, device=DEV)
+    run(logits_d.data_ptr(), bd.EPI_ARGMAX, keys=keys.data_ptr(), toks=tok_d.data_ptr())
+    logits = logits_d.cpu().numpy()
+    assert_close(logits, exp)
+    np.testing.assert_array_equal(tok_d.cpu().numpy(), logits.argmax(axis=1))
+
+
 def test_gemm_rejects_unsupported_shapes():
     a = bd.B2GemmArgs(16, 128, 16, 100, 32, 100, 128, 16, None, bd.W_F16, 0, None, None)  # K % 64
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
@@ -309,6 +363,9 @@ def test_gemm_rejects_unsupported_shapes():
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
     a = bd.B2GemmArgs(None, 0, 16, 128, 32, 128, 1000, 16, None, bd.W_F16, bd.EPI_ARGMAX, None, None)  # no keys
     assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
+    for split in (3, 16, 4):  # not a power of two <= 8; more CTAs than k stages (K = 128: 2 stages)
+        a = bd.B2GemmArgs(16, 128, 16, 128, 32, 128, 128, 16, None, bd.W_F16, 0, None, None, None, split)
+        assert bd.capi().b2_gemm(ctypes.byref(a), None) == -1
 
 
 def test_gemv_rejects_bad_shapes():
