@@ -199,6 +199,20 @@ int b2_attention(float* out, const float* q, int ldq, int M, int nq, int nkv, in
 int b2_attention_f16(uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
                      const B2KVRef* kv, void* work, int nsplit, b2_stream_t s);
 
+/* b2_attention for many sequences of different lengths: the cache positions
+ * [0, max_seq) are cut into fixed blocks of `block` positions (a multiple of
+ * 64) and each CTA streams one block of one (row, kv head) into shared memory
+ * by TMA, with scores and P.V on the tensor cores (FP16 Q and P, FP32 sums);
+ * blocks past a row's pos[m] are empty.  Strides multiples of 128 elements.  Writes out (FP32)
+ * or, when out16 is not NULL, FP16 rows instead.  work: device scratch of
+ * b2_attention_workspace(M, nq, hd, b2_attention_blocks_split(max_seq, block))
+ * bytes; K and V caches 16-byte aligned.  A bulk copy that does not arrive
+ * within the wait limit sets *err (device int) to 1 and leaves its rows
+ * unfinished. */
+int b2_attention_blocks_split(int max_seq, int block);
+int b2_attention_blocks(float* out, uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv, int hd,
+                        const B2KVRef* kv, void* work, int block, int* err, b2_stream_t s);
+
 /* lm_head + argmax over V rows of `table` (int8 [V][K] with FP32 scales,
  * F16 [V][K], or F32 [V][K]).  Input row m is RMSNorm(x[m]; norm_w, eps)
  * (norm_w may be NULL), rounded to FP16 for the int8 table (the reference's

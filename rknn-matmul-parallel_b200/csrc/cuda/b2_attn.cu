@@ -12,6 +12,7 @@
 // GQA group from registers, keeping an online (running max / running sum)
 // softmax.  Eight lanes cover one 128-wide row (16 dims each), so a 128-thread
 // CTA walks 16 positions per iteration.  A second kernel merges the ranges.
+#include <cuda.h>  // CUtensorMap
 #include <math.h>
 
 #include "b2_common.cuh"
@@ -237,6 +238,362 @@ extern "C" int b2_attention_f16(uint16_t* out16, const float* q, int ldq, int M,
     return attention_impl(nullptr, reinterpret_cast<__half*>(out16), q, ldq, M, nq, nkv, hd, kv, work, nsplit, s);
 }
 
+// ─── many sequences: fixed-size position blocks on the tensor cores (b2_attention_blocks) ───
+//
+// attention_f32 (src/cpu_ops.c:202-264) per row for batched decode, where the
+// rows have very different lengths.  Each CTA takes one block of `block`
+// consecutive cache positions of one (row, kv head), so the work per CTA does
+// not depend on the row's length and the grid's tail is short.  The block's
+// K and V rows stream through a ring of shared-memory stages by TMA (128-byte
+// swizzled boxes of 64 positions x 64 dims), and the four warps compute on
+// the stage before, each on 16 positions of a stage:
+//
+//   S^T = K Q^T    mma.sync m16n8k16: the warp's 16 positions are the M
+//                  rows, the GQA group's q heads the N columns (G <= 8, the
+//                  rest zero), head dims the K dimension;
+//   online softmax per q head over the 16 positions (8-lane shuffles);
+//   O^T += V^T P^T  the 128 head dims are M (8 tiles), the positions K; P^T
+//                  moves from the accumulator layout to the B-operand layout
+//                  with movmatrix.trans (FP16 P).
+//
+// Q and P are FP16, sums and the softmax FP32 (as in the prefill kernel).
+// Rows of a partial last stage are masked (V rows past the end are zeroed).
+namespace {
+
+constexpr int kBlkChunk = 64;                            // positions per stage (16 per warp)
+constexpr int kBlkStages = 3;
+constexpr int kBlkBox = 64 * 128;                        // one 64 x 64 FP16 box, bytes
+constexpr int kBlkStageBytes = 4 * kBlkBox;              // K dims 0-63, K 64-127, V 0-63, V 64-127
+constexpr long long kBlkWaitLimit = 1ll << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of (row r, 8-dim chunk c) in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads) attn_block_kernel(const __grid_constant__ CUtensorMap tk,
+                                                              const __grid_constant__ CUtensorMap tv,
+                                                              const float* __restrict__ q, int ldq, int nq, int nkv,
+                                                              B2KVRef kv, int block, float* __restrict__ part_ml,
+                                                              float* __restrict__ part_o, int nsplit,
+                                                              int* __restrict__ err) {
+    static_assert(G >= 1 && G <= 8, "GQA group must fit the 8 MMA columns");
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* ring =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t full[kBlkStages];
+    const int split = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    b2::pdl_trigger();
+    int seq = kv.rows_seq ? kv.rows_seq[m] : 0;
+    int L = kv.pos[m] + 1;
+    if (L < 1 || L > kv.max_seq || seq < 0 || seq >= kv.n_seqs) {  // invalid row: attend to nothing
+        L = 0;
+        seq = 0;
+    }
+    const int p0 = split * block;
+    const int p1 = min(L, p0 + block);
+    const int nchunks = p1 > p0 ? (p1 - p0 + kBlkChunk - 1) / kBlkChunk : 0;
+    // first cache row (of 128 dims) of this (sequence, layer, kv head)
+    const int row0 = (int)((seq * kv.seq_stride + kv.layer * kv.layer_stride + (long long)g * kv.max_seq * kHD) / kHD);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kBlkStages; s++)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[s])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tk) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tv) : "memory");
+    }
+    __syncthreads();
+    // The newest position's K and V come from the previous kernel.
+    b2::pdl_wait();
+    auto issue = [&](int c) {  // thread 0: chunk c of the block into stage c % kBlkStages
+        const int s = c % kBlkStages, y = row0 + p0 + c * kBlkChunk;
+        unsigned char* st = ring + s * kBlkStageBytes;
+        const uint32_t bar = smem_addr(&full[s]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBlkStageBytes)
+                     : "memory");
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+                "[%4];" ::"r"(smem_addr(st + i * kBlkBox)),
+                "l"(i < 2 ? &tk : &tv), "r"((i & 1) * 64), "r"(y), "r"(bar)
+                : "memory");
+    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < min(nchunks, kBlkStages); c++) issue(c);
+
+    // Q^T as the B operand of S^T = K Q^T: column n = lane / 4 is q head
+    // g*G + n (zero for n >= G); k step t covers dims 16t .. 16t+15.
+    uint32_t qb[8][2];
+    {
+        const int n = lane >> 2, d0 = 2 * (lane & 3);
+        const float* qp = q + (size_t)m * ldq + (size_t)(g * G + n) * kHD;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            if (n < G) {
+                qb[t][0] = pack_h2(qp[16 * t + d0], qp[16 * t + d0 + 1]);
+                qb[t][1] = pack_h2(qp[16 * t + d0 + 8], qp[16 * t + d0 + 9]);
+            } else {
+                qb[t][0] = qb[t][1] = 0u;
+            }
+        }
+    }
+    // O^T accumulator (8 tiles of 16 dims x 8 q columns), running max / sum
+    // of this lane's two columns j0 = 2 (lane % 4) and j0 + 1.
+    float o[8][4];
+#pragma unroll
+    for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+    float mx[2] = {-INFINITY, -INFINITY}, ls[2] = {0.f, 0.f};
+    const float scale = 1.0f / sqrtf((float)kHD);
+    const int pw = warp * 16;  // this warp's positions within a stage
+    bool ok = true;
+    int c = 0;
+    for (; c < nchunks; c++) {
+        const int s = c % kBlkStages, np = min(kBlkChunk, p1 - (p0 + c * kBlkChunk));
+        const uint32_t bar = smem_addr(&full[s]), par = (uint32_t)((c / kBlkStages) & 1);
+        uint32_t done = 0;
+        for (long long it = 0; ok && !done; it++) {
+            asm volatile(
+                "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
+                "p;\n}\n"
+                : "=r"(done)
+                : "r"(bar), "r"(par)
+                : "memory");
+            if (!done && it > kBlkWaitLimit) ok = false;
+        }
+        // one decision for the whole CTA, so every thread meets the same barriers
+        if (__syncthreads_or(!ok)) {
+            ok = false;
+            break;
+        }
+        unsigned char* st = ring + s * kBlkStageBytes;
+        const uint32_t sk = smem_addr(st), sv = smem_addr(st + 2 * kBlkBox);
+        if (np < kBlkChunk && pw + 16 > np) {
+            // V rows past the block's end may hold anything: zero this warp's
+            // (P is zero there, and 0 x inf would not be)
+            for (int r = max(pw, np) + (lane >> 4); r < pw + 16; r += 2) {
+                uint4* z = reinterpret_cast<uint4*>(st + 2 * kBlkBox + ((lane >> 3) & 1) * kBlkBox + r * 128) + (lane & 7);
+                *z = make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+        }
+        if (pw < np) {
+            // S^T [16 positions x 8 columns]
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                // A = K rows pw.., dims 16t..: sub-matrix j = lane / 8 -> (+8 rows if j odd, +8 dims if j >= 2)
+                const int r = pw + (lane & 7) + ((lane >> 3) & 1) * 8, d = 16 * t + (lane >> 4) * 8;
+                uint32_t a[4];
+                ldsm_x4(sk + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
+                mma16816(sc, a, qb[t][0], qb[t][1]);
+            }
+            // mask positions past the block, scale, online softmax per column
+            const int pa = pw + (lane >> 2), pb = pa + 8;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int pp = i < 2 ? pa : pb;
+                sc[i] = pp < np ? sc[i] * scale : -INFINITY;
+            }
+            float corr[2], pr[4];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                float cm = fmaxf(sc[j], sc[j + 2]);
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+                const float mn = fmaxf(mx[j], cm);
+                const bool none = mn == -INFINITY;
+                corr[j] = none ? 1.f : expf(mx[j] - mn);
+                pr[j] = none ? 0.f : expf(sc[j] - mn);
+                pr[j + 2] = none ? 0.f : expf(sc[j + 2] - mn);
+                float rs = pr[j] + pr[j + 2];
+                rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 16);
+                ls[j] = ls[j] * corr[j] + rs;
+                mx[j] = mn;
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                o[t][0] *= corr[0];
+                o[t][1] *= corr[1];
+                o[t][2] *= corr[0];
+                o[t][3] *= corr[1];
+            }
+            // P^T as the B operand: rows (positions) 0-7 and 8-15 transposed
+            const uint32_t pb0 = movm_t(pack_h2(pr[0], pr[1])), pb1 = movm_t(pack_h2(pr[2], pr[3]));
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                // A = V^T dims 16t.., positions pw..: sub-matrix j -> (+8 dims if j odd, +8 rows if j >= 2)
+                const int r = pw + (lane & 7) + (lane >> 4) * 8, d = 16 * t + ((lane >> 3) & 1) * 8;
+                uint32_t a[4];
+                ldsm_x4_t(sv + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
+                mma16816(o[t], a, pb0, pb1);
+            }
+        }
+        __syncthreads();  // every warp is done with stage s
+        if (threadIdx.x == 0 && c + kBlkStages < nchunks) issue(c + kBlkStages);
+    }
+    if (!ok) {
+        if ((threadIdx.x & 31) == 0) atomicExch(err, 1);
+        // chunks [c, c + kBlkStages) may still be landing in the ring: wait for
+        // them (again bounded) before the ring is reused or the CTA exits
+        if (threadIdx.x == 0) {
+            for (int cc = c; cc < min(nchunks, c + kBlkStages); cc++) {
+                const uint32_t bar = smem_addr(&full[cc % kBlkStages]), par = (uint32_t)((cc / kBlkStages) & 1);
+                uint32_t done = 0;
+                for (long long it = 0; !done && it <= kBlkWaitLimit; it++)
+                    asm volatile(
+                        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, "
+                        "1, 0, p;\n}\n"
+                        : "=r"(done)
+                        : "r"(bar), "r"(par)
+                        : "memory");
+            }
+        }
+    }
+    __syncthreads();  // the ring is idle: reuse it for the merge of the four warps
+    float* sm_m = reinterpret_cast<float*>(ring);  // [4 warps][8 columns]
+    float* sm_l = sm_m + 32;
+    float* sm_o = sm_l + 32;                       // [4 warps][G][kHD]
+    {
+        const int j0 = 2 * (lane & 3);
+        if (lane < 4) {
+            sm_m[warp * 8 + j0] = mx[0];
+            sm_m[warp * 8 + j0 + 1] = mx[1];
+            sm_l[warp * 8 + j0] = ls[0];
+            sm_l[warp * 8 + j0 + 1] = ls[1];
+        }
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            const int d = 16 * t + (lane >> 2);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int j = j0 + (i & 1), dd = d + (i >> 1) * 8;
+                if (j < G) sm_o[(warp * G + j) * kHD + dd] = o[t][i];
+            }
+        }
+    }
+    __syncthreads();
+    const int d = threadIdx.x;  // one thread per head dimension
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, sm_m[w * 8 + h]);
+        float lsum = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                if (sm_m[w * 8 + h] == -INFINITY) continue;
+                const float wt = expf(sm_m[w * 8 + h] - M);
+                lsum = fmaf(sm_l[w * 8 + h], wt, lsum);
+                acc = fmaf(sm_o[(w * G + h) * kHD + d], wt, acc);
+            }
+        }
+        const size_t slot = ((size_t)m * nq + g * G + h) * nsplit + split;
+        part_o[slot * kHD + d] = acc;
+        if (d == 0) {
+            part_ml[slot * 2] = M;
+            part_ml[slot * 2 + 1] = lsum;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" int b2_attention_blocks_split(int max_seq, int block) {
+    return block > 0 && block % kBlkChunk == 0 ? (max_seq + block - 1) / block : -1;
+}
+
+extern "C" int b2_attention_blocks(float* out, uint16_t* out16, const float* q, int ldq, int M, int nq, int nkv,
+                                   int hd, const B2KVRef* kv, void* work, int block, int* err, b2_stream_t s) {
+    if (M <= 0) return 0;
+    if (hd != kHD) return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_blocks: head_dim %d != 128", hd);
+    if ((!out && !out16) || !q || !kv || !kv->pos || !work || !err || nkv <= 0 || nq % nkv != 0 ||
+        block <= 0 || block % kBlkChunk != 0 || kv->max_seq <= 0 || kv->n_seqs <= 0 ||
+        (reinterpret_cast<uintptr_t>(kv->k_base) & 15) || (reinterpret_cast<uintptr_t>(kv->v_base) & 15) ||
+        kv->seq_stride % kHD || kv->layer_stride % kHD)
+        return b2_set_error(B2_ERR_INVALID_ARG,
+                            "b2_attention_blocks: bad arguments (block %% %d, 16-byte caches, strides %% 128)",
+                            kBlkChunk);
+    const int nsplit = (kv->max_seq + block - 1) / block;
+    // rows of 128 dims the caches span for these rows (reads past it are zero-filled)
+    const long long rows = ((long long)(kv->n_seqs - 1) * kv->seq_stride + (long long)kv->layer * kv->layer_stride +
+                            (long long)nkv * kv->max_seq * kHD) / kHD;
+    if (rows >= (1ll << 31)) return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_blocks: cache too large");
+    CUtensorMap tk, tv;
+    int rc = b2_tensor_map_f16(&tk, kv->k_base, kHD, (uint64_t)rows, kHD * 2, 64, 64);
+    if (!rc) rc = b2_tensor_map_f16(&tv, kv->v_base, kHD, (uint64_t)rows, kHD * 2, 64, 64);
+    if (rc) return rc;
+    float* part_ml = reinterpret_cast<float*>(work);
+    float* part_o = part_ml + (size_t)M * nq * nsplit * 2;
+    dim3 grid(nsplit, nkv, M);
+    cudaStream_t st = (cudaStream_t)s;
+    constexpr size_t smem = (size_t)kBlkStages * kBlkStageBytes + 1024;
+    static_assert((size_t)kBlkStages * kBlkStageBytes >= (64 + 4 * 8 * kHD) * sizeof(float),
+                  "merge scratch exceeds the ring");
+    cudaError_t e = cudaSuccess;
+    {  // more than the default 48 KB of dynamic shared memory: opt in once per device
+        static bool set[8] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!set[dev & 7]) {
+            e = cudaFuncSetAttribute(attn_block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(attn_block_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(attn_block_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess)
+                return b2_set_error(B2_ERR_CUDA, "b2_attention_blocks smem attr: %s", cudaGetErrorString(e));
+            set[dev & 7] = true;
+        }
+    }
+    switch (nq / nkv) {
+        case 1: e = b2::launch_pdl(attn_block_kernel<1>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        case 2: e = b2::launch_pdl(attn_block_kernel<2>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        case 4: e = b2::launch_pdl(attn_block_kernel<4>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        default: return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_blocks: GQA group %d not in {1,2,4}", nq / nkv);
+    }
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention_blocks: %s", cudaGetErrorString(e));
+    e = b2::launch_pdl(attn_combine_kernel, dim3(nq, M), dim3(kHD), 0, st, out, reinterpret_cast<__half*>(out16), nq,
+                       (const float*)part_ml, (const float*)part_o, nsplit);
+    if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention_blocks combine: %s", cudaGetErrorString(e));
+    return 0;
+}
+
 // ─── causal flash attention for batch prefill (b2_attention_prefill) ───
 //
 // attention_batch_causal_f32 (src/cpu_ops.c:459-571) for M consecutive rows
@@ -260,9 +617,6 @@ constexpr int kFaKv = 64;              // positions per K/V block
 constexpr int kFaPad = kHD + 8;        // padded row (halves)
 constexpr int kFaThreads = 128;
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -282,10 +636,6 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
 }
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
 }
 
 template <int G>

@@ -14,6 +14,11 @@
 // Records an error message for b2_last_error(); defined in b2_runtime.cu.
 int b2_set_error(int code, const char* fmt, ...);
 int b2_check_launch(const char* what);
+// 2-D FP16 tensor map (CUtensorMap, 64 bytes) over [outer][inner] rows
+// row_bytes apart, boxes of box_outer x box_inner elements with the 128-byte
+// swizzle; defined in b2_gemm.cu.
+int b2_tensor_map_f16(void* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                      uint32_t box_inner, uint32_t box_outer);
 
 #define B2_TRY(expr)                                                                   \
     do {                                                                               \

@@ -718,6 +718,12 @@ int by_wtype(const B2GemmArgs* a, cudaStream_t s, int sms) {
 
 }  // namespace
 
+// FP16 2-D tensor map with the 128-byte swizzle for other kernels of the library.
+int b2_tensor_map_f16(void* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                      uint32_t box_inner, uint32_t box_outer) {
+    return make_map(reinterpret_cast<CUtensorMap*>(map), base, true, inner, outer, row_bytes, box_inner, box_outer);
+}
+
 extern "C" size_t b2_gemm_argmax_keys(int M, int N) { return (size_t)M * ((N + kBM - 1) / kBM) * 8; }
 
 extern "C" int b2_gemm(const B2GemmArgs* a, b2_stream_t stream) {

@@ -20,6 +20,8 @@
 struct MatmulDecoderBatch {
     DevModel model;
     int device, n, max_seq, split;
+    int attn_block; /* > 0: attention in blocks of this many positions (b2_attention_blocks) */
+    int ws_split;   /* position ranges the attention workspace is sized for */
     b2_stream_t stream;
     uint16_t *k_cache, *v_cache;
     long long seq_stride, layer_stride;
@@ -28,7 +30,7 @@ struct MatmulDecoderBatch {
     uint16_t* x16b;               /* [n][ffn] FP16 gate|up output for the down-projection GEMM */
     unsigned long long* lm_keys;  /* per-CTA argmax keys of the tensor-core lm_head */
     int *d_blk;   /* [0,n) tokens, [n,2n) positions, [2n,3n) row->sequence */
-    int *d_tok;
+    int *d_tok;   /* [0,n) next tokens, [n] attention error flag */
     void *attn_work, *lm_work;
     int *h_blk, *h_tok;
     int* seq_len;
@@ -99,12 +101,24 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     if (es && atoi(es) > 0) b->split = atoi(es);
     if (b->split < 1) b->split = 1;
     if (b->split > 64) b->split = 64;
+    /* Attention in fixed blocks of positions streamed by bulk copies: the
+     * work per CTA does not depend on the sequence lengths (B2_BATCH_BLOCK,
+     * a multiple of 64; 0 keeps the per-sequence ranges above). */
+    b->attn_block = 1024;
+    const char* eb = getenv("B2_BATCH_BLOCK");
+    if (eb) b->attn_block = atoi(eb);
+    if (b->attn_block < 0 || b->attn_block % 64) b->attn_block = 1024;
+    b->ws_split = b->split;
+    if (b->attn_block > 0) {
+        const int bs = b2_attention_blocks_split(max_seq_len, b->attn_block);
+        if (bs > b->ws_split) b->ws_split = bs;
+    }
     b2_get_device(&b->device);
     b->seq_len = (int*)calloc((size_t)n_seqs, sizeof(int));
     int rc = b->seq_len ? 0 : MATMUL_DECODER_ERR_MEMORY;
     if (!rc)
         rc = md_model_load_dir(&b->model, model_dir, &cfg, quant_type, max_seq_len,
-                               batch_bytes(&cfg, n_seqs, max_seq_len, b->split));
+                               batch_bytes(&cfg, n_seqs, max_seq_len, b->ws_split));
     if (rc) {
         MD_LOG("batch_create failed (%d)\n", rc);
         matmul_decoder_batch_destroy(b);
@@ -125,8 +139,8 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     b->act = (float*)md_arena_alloc(&m->arena, n * F * 4);
     b->logits = (float*)md_arena_alloc(&m->arena, n * c->vocab_size * 4);
     b->d_blk = (int*)md_arena_alloc(&m->arena, n * 3 * 4);
-    b->d_tok = (int*)md_arena_alloc(&m->arena, n * 4);
-    b->attn_work = md_arena_alloc(&m->arena, b2_attention_workspace(n_seqs, c->num_q_heads, (int)hd, b->split));
+    b->d_tok = (int*)md_arena_alloc(&m->arena, (n + 1) * 4);
+    b->attn_work = md_arena_alloc(&m->arena, b2_attention_workspace(n_seqs, c->num_q_heads, (int)hd, b->ws_split));
     b->lm_work = md_arena_alloc(&m->arena, b2_lm_head_workspace(n_seqs, c->vocab_size));
     {
         const size_t kmax = H > qd ? (H > F ? H : F) : (qd > F ? qd : F);
@@ -143,7 +157,9 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     if (!rc) rc = b2_stream_create(&b->stream);
     for (int i = 0; i < 3 && !rc; i++) rc = b2_event_create(&b->ev[i]);
     if (!rc) rc = b2_host_alloc((void**)&b->h_blk, n * 3 * 4);
-    if (!rc) rc = b2_host_alloc((void**)&b->h_tok, n * 4);
+    if (!rc) rc = b2_host_alloc((void**)&b->h_tok, (n + 1) * 4);
+    if (!rc) rc = b2_memset(b->d_tok, 0, (n + 1) * 4, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
     if (rc) {
         MD_LOG("batch_create allocation failed (%d): %s\n", rc, b2_last_error());
         matmul_decoder_batch_destroy(b);
@@ -203,7 +219,8 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
     if (!rc) rc = b2_embed(b->hidden, m->emb, b->d_blk, NULL, NULL, n, H, s);
     B2KVRef kv = {b->k_cache, b->v_cache, b->seq_stride, b->layer_stride, 0, b->max_seq, b->d_blk + 2 * n,
                   b->d_blk + n, n};
-    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16, b->x16b, -1};
+    LayerBuffers lb = {b->hidden, b->qkv, b->attn, b->act, b->attn_work, b->split, b->x16, b->x16b, -1,
+                       b->attn_block, b->d_tok + n};
     if (!rc) rc = md_enqueue_layers(m, &lb, n, &kv, s);
     if (!rc) rc = b2_event_record(b->ev[1], s);
     if (!rc && b->x16 && n >= 16 && (m->lm_wtype == B2_W_I8 || m->lm_wtype == B2_W_F16) && H % 64 == 0) {
@@ -216,7 +233,7 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
         rc = b2_lm_head_argmax(b->hidden, H, n, H, c->vocab_size, m->lm, m->lm_scales, m->lm_wtype, m->final_norm,
                                c->rms_eps, b->logits, c->vocab_size, b->d_tok, b->lm_work, s);
     }
-    if (!rc) rc = b2_memcpy_d2h(b->h_tok, b->d_tok, (size_t)n * 4, s);
+    if (!rc) rc = b2_memcpy_d2h(b->h_tok, b->d_tok, (size_t)(n + 1) * 4, s);
     if (!rc) rc = b2_event_record(b->ev[2], s);
     return rc;
 }
@@ -256,6 +273,12 @@ int matmul_decoder_batch_step(MatmulDecoderBatch* b, const int* tokens_in, int* 
     if (rc) {
         MD_LOG("batch step failed: %s\n", b2_last_error());
         return rc;
+    }
+    if (b->h_tok[b->n]) {  /* a bulk copy of the attention did not arrive in time */
+        MD_LOG("batch step: attention wait limit reached\n");
+        b2_memset(b->d_tok + b->n, 0, 4, b->stream);
+        b2_stream_sync(b->stream);
+        return MATMUL_DECODER_ERR_RKNN;
     }
     double t_copy = 0;
     if (logits_out) {

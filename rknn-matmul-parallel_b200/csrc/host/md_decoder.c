@@ -374,7 +374,7 @@ static int enqueue_token(MatmulDecoderContext* ctx, int with_head, const void* t
         rc = b2_embed(ctx->hidden, m->emb, ctx->d_blk, ctx->d_blk + 1, (const float*)(ctx->d_blk + PARAMS_INTS),
                       1, H, s);
     B2KVRef kv = kv_ref(ctx, ctx->d_blk + 4);
-    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1};
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1, 0, NULL};
     if (!rc) rc = md_enqueue_layers(m, &lb, 1, &kv, s);
     if (!rc) rc = b2_event_record(ctx->ev[1], s);
     if (!rc && with_head) {
@@ -575,7 +575,7 @@ static int build_loop_graph(MatmulDecoderContext* ctx) {
     if (rc) return rc;
     int rc2 = b2_embed(ctx->hidden, m->emb, ctx->d_loop, NULL, NULL, 1, H, s);
     B2KVRef kv = kv_ref(ctx, ctx->d_loop + 1);
-    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1};
+    LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, ctx->split_decode, NULL, NULL, -1, 0, NULL};
     if (!rc2) rc2 = md_enqueue_layers(m, &lb, 1, &kv, s);
     if (!rc2)
         rc2 = b2_lm_head_argmax(ctx->hidden, H, 1, H, m->cfg.vocab_size, m->lm, m->lm_scales, m->lm_wtype,
@@ -680,7 +680,7 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
         if (split < 1) split = 1;
         if (split > ctx->split_decode) split = ctx->split_decode;
         LayerBuffers lb = {ctx->hidden, ctx->qkv, ctx->attn, ctx->act, ctx->attn_work, split, ctx->x16,
-                           ctx->x16b, ctx->seq_len};
+                           ctx->x16b, ctx->seq_len, 0, NULL};
         if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
         if (!rc) rc = md_enqueue_layers(m, &lb, rows, &kv, ctx->stream);
         if (!rc) rc = b2_event_record(ctx->ev[1], ctx->stream);

@@ -98,6 +98,8 @@ typedef struct {
     uint16_t* x16;   /* [M][max(H, qd, ffn)] FP16 staging for the tensor-core GEMM, or NULL */
     uint16_t* x16b;  /* [M][ffn] FP16 gate|up output = down-projection input, or NULL */
     int prefill_base; /* >= 0: the M rows are one sequence at positions prefill_base + m (flash attention) */
+    int attn_block;   /* > 0: attention in fixed blocks of this many positions (b2_attention_blocks) */
+    int* attn_err;    /* device flag for b2_attention_blocks */
 } LayerBuffers;
 int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2KVRef* kv_proto,
                       b2_stream_t s);

@@ -89,6 +89,9 @@ int md_enqueue_layers(const DevModel* m, const LayerBuffers* b, int M, const B2K
         uint16_t* attn16 = o_tc ? b->x16 : NULL;
         if (b->prefill_base >= 0 && M >= MD_GEMM_MIN_ROWS && nq == 2 * nkv && hd == 128 && !kv.rows_seq)
             rc = b2_attention_prefill(attn32, attn16, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->prefill_base, s);
+        else if (b->attn_block > 0)
+            rc = b2_attention_blocks(attn32, attn16, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_block,
+                                     b->attn_err, s);
         else if (o_tc)
             rc = b2_attention_f16(attn16, b->qkv, ldqkv, M, nq, nkv, hd, &kv, b->attn_work, b->attn_split, s);
         else

@@ -137,6 +137,9 @@ SIGNATURES = {
     "b2_attention_workspace": (c_size, [c_int, c_int, c_int, c_int]),
     "b2_attention": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp]),
     "b2_attention_f16": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp]),
+    "b2_attention_blocks_split": (c_int, [c_int, c_int]),
+    "b2_attention_blocks": (c_int, [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp,
+                                    c_vp]),
     "b2_lm_head_workspace": (c_size, [c_int, c_int]),
     "b2_loop_advance": (c_int, [c_vp, c_vp, c_int, c_vp]),
     "b2_lm_head_noalloc_max_keys": (c_size, []),

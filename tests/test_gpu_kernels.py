@@ -442,6 +442,57 @@ def test_attention_rows_and_sequences(G):
             assert_close(out[m], exp, rtol=1e-3, atol=1e-4)
 
 
+@pytest.mark.parametrize("G", [1, 2, 4])
+@pytest.mark.parametrize("block", [64, 256])
+def test_attention_blocks_rows_and_sequences(G, block):
+    """Batched-decode attention in fixed position blocks (TMA into a
+    shared-memory ring, scores and P.V on the tensor cores with FP16 Q and P)
+    against the oracle: rows of different sequences and lengths, including
+    partial last stages and blocks past a row's end, in FP32 and FP16 output."""
+    nkv, hd, max_seq = 8, 128, 4100
+    nq = nkv * G
+    rng = np.random.default_rng(90 + G + block)
+    n_seq = 3
+    kc = rng.standard_normal((n_seq, nkv, max_seq, hd), dtype=np.float32).astype(np.float16)
+    vc = rng.standard_normal((n_seq, nkv, max_seq, hd), dtype=np.float32).astype(np.float16)
+    rows_seq = np.array([0, 2, 1, 2, 0, 1], np.int32)
+    pos = np.array([0, 1, 31, 127, 1000, 4095], np.int32)
+    M = len(pos)
+    q = rng.standard_normal((M, nq * hd), dtype=np.float32)
+    kc_d, vc_d, q_d = dev(kc), dev(vc), dev(q)
+    nsplit = bd.capi().b2_attention_blocks_split(max_seq, block)
+    assert nsplit == -(-max_seq // block)
+    work = torch.empty(bd.capi().b2_attention_workspace(M, nq, hd, nsplit), dtype=torch.uint8, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv = kv_ref(kc_d, vc_d, 0, max_seq, dev(pos), dev(rows_seq), seq_stride=nkv * max_seq * hd, n_seqs=n_seq)
+    out_d = torch.empty((M, nq * hd), dtype=torch.float32, device=DEV)
+    bd.check(bd.capi().b2_attention_blocks(out_d.data_ptr(), None, q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
+                                           ctypes.byref(kv), work.data_ptr(), block, err.data_ptr(), stream()),
+             "attention_blocks")
+    out_h = torch.empty((M, nq * hd), dtype=torch.float16, device=DEV)
+    bd.check(bd.capi().b2_attention_blocks(None, out_h.data_ptr(), q_d.data_ptr(), nq * hd, M, nq, nkv, hd,
+                                           ctypes.byref(kv), work.data_ptr(), block, err.data_ptr(), stream()),
+             "attention_blocks f16")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    out = out_d.cpu().numpy()
+    np.testing.assert_array_equal(out_h.cpu().numpy(), out.astype(np.float16))
+    for m in range(M):
+        sq, L = rows_seq[m], pos[m] + 1
+        kk = kc[sq, :, :L].transpose(1, 0, 2).astype(np.float32)
+        vv = vc[sq, :, :L].transpose(1, 0, 2).astype(np.float32)
+        assert_close(out[m], ref.attention(q[m], kk, vv, nq, nkv, hd), rtol=2e-2, atol=5e-3)
+
+
+def test_attention_blocks_rejects_bad_arguments():
+    kv = bd.B2KVRef(16, 16, 0, 0, 0, 64, None, 16, 1)
+    assert bd.capi().b2_attention_blocks_split(4096, 96) == -1  # not a multiple of 64
+    assert bd.capi().b2_attention_blocks(16, None, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 16, 100, 16, None) == -1
+    assert bd.capi().b2_attention_blocks(16, None, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 16, 64, None, None) == -1
+    kv = bd.B2KVRef(24, 16, 0, 0, 0, 64, None, 16, 1)  # K cache not 16-byte aligned
+    assert bd.capi().b2_attention_blocks(16, None, 16, 2048, 8, 16, 8, 128, ctypes.byref(kv), 16, 64, 16, None) == -1
+
+
 @pytest.mark.parametrize("M, base", [(16, 0), (60, 0), (77, 100), (512, 0), (200, 3000)])
 def test_attention_prefill_flash_matches_oracle(M, base):
     """Causal flash attention of a prefill chunk (tensor cores, FP16 Q and P)
