@@ -203,7 +203,9 @@ int b2_attention_f16(uint16_t* out16, const float* q, int ldq, int M, int nq, in
  * [0, max_seq) are cut into fixed blocks of `block` positions (a multiple of
  * 64) and each CTA streams one block of one (row, kv head) into shared memory
  * by TMA, with scores and P.V on the tensor cores (FP16 Q and P, FP32 sums);
- * blocks past a row's pos[m] are empty.  Strides multiples of 128 elements.  Writes out (FP32)
+ * blocks past a row's pos[m] are empty.  Persistent: two CTAs per SM walk the
+ * rows' blocks, so the grid does not depend on the lengths.  M <= 512; strides
+ * multiples of 128 elements.  Writes out (FP32)
  * or, when out16 is not NULL, FP16 rows instead.  work: device scratch of
  * b2_attention_workspace(M, nq, hd, b2_attention_blocks_split(max_seq, block))
  * bytes; K and V caches 16-byte aligned.  A bulk copy that does not arrive

@@ -168,25 +168,35 @@ __global__ void __launch_bounds__(kThreads) attn_split_kernel(const float* __res
     }
 }
 
+// Merges the nsplit partial (max, sum, output) slots of each (row, q head).
+// With block > 0 (b2_attention_blocks) only the slots of the row's blocks,
+// ceil((pos[m] + 1) / block), were written.
 __global__ void __launch_bounds__(kHD) attn_combine_kernel(float* __restrict__ out, __half* __restrict__ out16,
                                                            int nq, const float* __restrict__ part_ml,
-                                                           const float* __restrict__ part_o, int nsplit) {
+                                                           const float* __restrict__ part_o, int nsplit,
+                                                           const int* __restrict__ pos, int block, int max_seq) {
     b2::pdl_trigger();
     b2::pdl_wait();
     const int h = blockIdx.x, m = blockIdx.y, d = threadIdx.x;
     const size_t base = ((size_t)m * nq + h) * nsplit;
+    int ns = nsplit;
+    if (block > 0) {
+        const int L = pos[m] + 1;
+        ns = (L < 1 || L > max_seq) ? 0 : min(nsplit, (L + block - 1) / block);
+    }
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
+    for (int s = 0; s < ns; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; s++) {
+    for (int s = 0; s < ns; s++) {
         const float ms = part_ml[(base + s) * 2];
         if (ms == -INFINITY) continue;
         const float w = expf(ms - M);
         den = fmaf(part_ml[(base + s) * 2 + 1], w, den);
         num = fmaf(part_o[(base + s) * kHD + d], w, num);
     }
-    if (out16) out16[((size_t)m * nq + h) * kHD + d] = __float2half_rn(num / den);
-    else out[((size_t)m * nq + h) * kHD + d] = num / den;
+    const float r = den > 0.f ? num / den : 0.f;  // a row that attends to nothing gives zeros
+    if (out16) out16[((size_t)m * nq + h) * kHD + d] = __float2half_rn(r);
+    else out[((size_t)m * nq + h) * kHD + d] = r;
 }
 
 int pick_split(int M, int nkv, int nsplit) {
@@ -223,7 +233,7 @@ static int attention_impl(float* out, __half* out16, const float* q, int ldq, in
     }
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention split: %s", cudaGetErrorString(e));
     e = b2::launch_pdl(attn_combine_kernel, dim3(nq, M), dim3(kHD), 0, st, out, out16, nq, (const float*)part_ml,
-                       (const float*)part_o, nsplit);
+                       (const float*)part_o, nsplit, (const int*)nullptr, 0, 0);
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention combine: %s", cudaGetErrorString(e));
     return 0;
 }
@@ -300,32 +310,78 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+constexpr int kBlkMaxRows = 512;  // rows one launch takes (the per-row unit prefix lives in shared memory)
+
+// One unit of work: block b of row m, kv head g (positions [p0, p1)).
+struct BlkUnit {
+    int m, g, b, p0, p1, nch, row0;
+};
+
+// Unit u of the launch: units are ordered by row, then kv head, then block;
+// pre[m] is the number of units of rows < m.
+__device__ __forceinline__ BlkUnit blk_unit(int u, const int* pre, int M, int nkv, int block, const B2KVRef& kv) {
+    int lo = 0, hi = M;  // largest m with pre[m] <= u
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (pre[mid] <= u) lo = mid;
+        else hi = mid;
+    }
+    BlkUnit x;
+    x.m = lo;
+    const int nb = (pre[lo + 1] - pre[lo]) / nkv, r = u - pre[lo];
+    x.g = r / nb;
+    x.b = r % nb;
+    const int L = kv.pos[lo] + 1;
+    const int seq = kv.rows_seq ? kv.rows_seq[lo] : 0;
+    x.p0 = x.b * block;
+    x.p1 = min(L, x.p0 + block);
+    x.nch = (x.p1 - x.p0 + kBlkChunk - 1) / kBlkChunk;
+    x.row0 = (int)((seq * kv.seq_stride + kv.layer * kv.layer_stride + (long long)x.g * kv.max_seq * kHD) / kHD);
+    return x;
+}
+
+// Persistent: CTA i takes units i, i + gridDim.x, ...  Thread 0 keeps the
+// ring kBlkStages chunks ahead of the warps, across unit boundaries, so the
+// memory pipe does not drain between units.
 template <int G>
 __global__ void __launch_bounds__(kThreads) attn_block_kernel(const __grid_constant__ CUtensorMap tk,
                                                               const __grid_constant__ CUtensorMap tv,
-                                                              const float* __restrict__ q, int ldq, int nq, int nkv,
-                                                              B2KVRef kv, int block, float* __restrict__ part_ml,
-                                                              float* __restrict__ part_o, int nsplit,
-                                                              int* __restrict__ err) {
+                                                              const float* __restrict__ q, int ldq, int M, int nq,
+                                                              int nkv, B2KVRef kv, int block,
+                                                              float* __restrict__ part_ml, float* __restrict__ part_o,
+                                                              int nsplit, int* __restrict__ err) {
     static_assert(G >= 1 && G <= 8, "GQA group must fit the 8 MMA columns");
     extern __shared__ unsigned char smem_raw[];
     unsigned char* ring =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t full[kBlkStages];
-    const int split = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+    __shared__ int pre[kBlkMaxRows + 1];
+    __shared__ float mg_m[4][8], mg_l[4][8];
+    __shared__ float mg_o[4][G][kHD];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     b2::pdl_trigger();
-    int seq = kv.rows_seq ? kv.rows_seq[m] : 0;
-    int L = kv.pos[m] + 1;
-    if (L < 1 || L > kv.max_seq || seq < 0 || seq >= kv.n_seqs) {  // invalid row: attend to nothing
-        L = 0;
-        seq = 0;
+    // units per row: ceil(L / block) blocks per kv head (none for an invalid
+    // row); positions and rows are written before the step's first kernel
+    if (warp == 0) {
+        int carry = 0;
+        for (int base = 0; base < M; base += 32) {
+            const int m = base + lane;
+            int n = 0;
+            if (m < M) {
+                const int L = kv.pos[m] + 1, seq = kv.rows_seq ? kv.rows_seq[m] : 0;
+                if (L >= 1 && L <= kv.max_seq && seq >= 0 && seq < kv.n_seqs) n = (L + block - 1) / block * nkv;
+            }
+            int incl = n;  // inclusive warp scan
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            if (m < M) pre[m + 1] = carry + incl;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) pre[0] = 0;
     }
-    const int p0 = split * block;
-    const int p1 = min(L, p0 + block);
-    const int nchunks = p1 > p0 ? (p1 - p0 + kBlkChunk - 1) / kBlkChunk : 0;
-    // first cache row (of 128 dims) of this (sequence, layer, kv head)
-    const int row0 = (int)((seq * kv.seq_stride + kv.layer * kv.layer_stride + (long long)g * kv.max_seq * kHD) / kHD);
     if (threadIdx.x == 0) {
         for (int s = 0; s < kBlkStages; s++)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[s])) : "memory");
@@ -334,10 +390,18 @@ __global__ void __launch_bounds__(kThreads) attn_block_kernel(const __grid_const
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tv) : "memory");
     }
     __syncthreads();
-    // The newest position's K and V come from the previous kernel.
+    const int U = pre[M];
+    // The newest position's K and V come from the previous kernel (every CTA
+    // waits, so this grid never completes before its predecessor).
     b2::pdl_wait();
-    auto issue = [&](int c) {  // thread 0: chunk c of the block into stage c % kBlkStages
-        const int s = c % kBlkStages, y = row0 + p0 + c * kBlkChunk;
+    if ((int)blockIdx.x >= U) return;
+
+    // producer cursor (thread 0 only): next chunk to request
+    int iu = blockIdx.x, ic = 0, kin = 0;
+    BlkUnit iun = blk_unit(iu, pre, M, nkv, block, kv);
+    auto issue_next = [&]() {
+        if (iu >= U) return;
+        const int s = kin % kBlkStages, y = iun.row0 + iun.p0 + ic * kBlkChunk;
         unsigned char* st = ring + s * kBlkStageBytes;
         const uint32_t bar = smem_addr(&full[s]);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBlkStageBytes)
@@ -349,130 +413,187 @@ __global__ void __launch_bounds__(kThreads) attn_block_kernel(const __grid_const
                 "[%4];" ::"r"(smem_addr(st + i * kBlkBox)),
                 "l"(i < 2 ? &tk : &tv), "r"((i & 1) * 64), "r"(y), "r"(bar)
                 : "memory");
+        kin++;
+        if (++ic == iun.nch) {
+            ic = 0;
+            iu += gridDim.x;
+            if (iu < U) iun = blk_unit(iu, pre, M, nkv, block, kv);
+        }
     };
     if (threadIdx.x == 0)
-        for (int c = 0; c < min(nchunks, kBlkStages); c++) issue(c);
+        for (int i = 0; i < kBlkStages; i++) issue_next();
 
-    // Q^T as the B operand of S^T = K Q^T: column n = lane / 4 is q head
-    // g*G + n (zero for n >= G); k step t covers dims 16t .. 16t+15.
-    uint32_t qb[8][2];
-    {
-        const int n = lane >> 2, d0 = 2 * (lane & 3);
-        const float* qp = q + (size_t)m * ldq + (size_t)(g * G + n) * kHD;
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            if (n < G) {
-                qb[t][0] = pack_h2(qp[16 * t + d0], qp[16 * t + d0 + 1]);
-                qb[t][1] = pack_h2(qp[16 * t + d0 + 8], qp[16 * t + d0 + 9]);
-            } else {
-                qb[t][0] = qb[t][1] = 0u;
-            }
-        }
-    }
-    // O^T accumulator (8 tiles of 16 dims x 8 q columns), running max / sum
-    // of this lane's two columns j0 = 2 (lane % 4) and j0 + 1.
-    float o[8][4];
-#pragma unroll
-    for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
-    float mx[2] = {-INFINITY, -INFINITY}, ls[2] = {0.f, 0.f};
     const float scale = 1.0f / sqrtf((float)kHD);
     const int pw = warp * 16;  // this warp's positions within a stage
+    uint32_t qb[8][2];
+    float o[8][4], mx[2], ls[2];
     bool ok = true;
-    int c = 0;
-    for (; c < nchunks; c++) {
-        const int s = c % kBlkStages, np = min(kBlkChunk, p1 - (p0 + c * kBlkChunk));
-        const uint32_t bar = smem_addr(&full[s]), par = (uint32_t)((c / kBlkStages) & 1);
-        uint32_t done = 0;
-        for (long long it = 0; ok && !done; it++) {
-            asm volatile(
-                "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
-                "p;\n}\n"
-                : "=r"(done)
-                : "r"(bar), "r"(par)
-                : "memory");
-            if (!done && it > kBlkWaitLimit) ok = false;
-        }
-        // one decision for the whole CTA, so every thread meets the same barriers
-        if (__syncthreads_or(!ok)) {
-            ok = false;
-            break;
-        }
-        unsigned char* st = ring + s * kBlkStageBytes;
-        const uint32_t sk = smem_addr(st), sv = smem_addr(st + 2 * kBlkBox);
-        if (np < kBlkChunk && pw + 16 > np) {
-            // V rows past the block's end may hold anything: zero this warp's
-            // (P is zero there, and 0 x inf would not be)
-            for (int r = max(pw, np) + (lane >> 4); r < pw + 16; r += 2) {
-                uint4* z = reinterpret_cast<uint4*>(st + 2 * kBlkBox + ((lane >> 3) & 1) * kBlkBox + r * 128) + (lane & 7);
-                *z = make_uint4(0, 0, 0, 0);
-            }
-            __syncwarp();
-        }
-        if (pw < np) {
-            // S^T [16 positions x 8 columns]
-            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    int kout = 0;  // chunks consumed
+    for (int cu = blockIdx.x; cu < U && ok; cu += gridDim.x) {
+        const BlkUnit un = blk_unit(cu, pre, M, nkv, block, kv);
+        // Q^T as the B operand of S^T = K Q^T: column n = lane / 4 is q head
+        // g*G + n (zero for n >= G); k step t covers dims 16t .. 16t+15.
+        {
+            const int n = lane >> 2, d0 = 2 * (lane & 3);
+            const float* qp = q + (size_t)un.m * ldq + (size_t)(un.g * G + n) * kHD;
 #pragma unroll
             for (int t = 0; t < 8; t++) {
-                // A = K rows pw.., dims 16t..: sub-matrix j = lane / 8 -> (+8 rows if j odd, +8 dims if j >= 2)
-                const int r = pw + (lane & 7) + ((lane >> 3) & 1) * 8, d = 16 * t + (lane >> 4) * 8;
-                uint32_t a[4];
-                ldsm_x4(sk + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
-                mma16816(sc, a, qb[t][0], qb[t][1]);
-            }
-            // mask positions past the block, scale, online softmax per column
-            const int pa = pw + (lane >> 2), pb = pa + 8;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int pp = i < 2 ? pa : pb;
-                sc[i] = pp < np ? sc[i] * scale : -INFINITY;
-            }
-            float corr[2], pr[4];
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                float cm = fmaxf(sc[j], sc[j + 2]);
-                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-                const float mn = fmaxf(mx[j], cm);
-                const bool none = mn == -INFINITY;
-                corr[j] = none ? 1.f : expf(mx[j] - mn);
-                pr[j] = none ? 0.f : expf(sc[j] - mn);
-                pr[j + 2] = none ? 0.f : expf(sc[j + 2] - mn);
-                float rs = pr[j] + pr[j + 2];
-                rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-                rs += __shfl_xor_sync(0xffffffffu, rs, 8);
-                rs += __shfl_xor_sync(0xffffffffu, rs, 16);
-                ls[j] = ls[j] * corr[j] + rs;
-                mx[j] = mn;
-            }
-#pragma unroll
-            for (int t = 0; t < 8; t++) {
-                o[t][0] *= corr[0];
-                o[t][1] *= corr[1];
-                o[t][2] *= corr[0];
-                o[t][3] *= corr[1];
-            }
-            // P^T as the B operand: rows (positions) 0-7 and 8-15 transposed
-            const uint32_t pb0 = movm_t(pack_h2(pr[0], pr[1])), pb1 = movm_t(pack_h2(pr[2], pr[3]));
-#pragma unroll
-            for (int t = 0; t < 8; t++) {
-                // A = V^T dims 16t.., positions pw..: sub-matrix j -> (+8 dims if j odd, +8 rows if j >= 2)
-                const int r = pw + (lane & 7) + (lane >> 4) * 8, d = 16 * t + ((lane >> 3) & 1) * 8;
-                uint32_t a[4];
-                ldsm_x4_t(sv + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
-                mma16816(o[t], a, pb0, pb1);
+                if (n < G) {
+                    qb[t][0] = pack_h2(qp[16 * t + d0], qp[16 * t + d0 + 1]);
+                    qb[t][1] = pack_h2(qp[16 * t + d0 + 8], qp[16 * t + d0 + 9]);
+                } else {
+                    qb[t][0] = qb[t][1] = 0u;
+                }
             }
         }
-        __syncthreads();  // every warp is done with stage s
-        if (threadIdx.x == 0 && c + kBlkStages < nchunks) issue(c + kBlkStages);
+        // O^T accumulator (8 tiles of 16 dims x 8 q columns), running max /
+        // sum of this lane's two columns j0 = 2 (lane % 4) and j0 + 1.
+#pragma unroll
+        for (int t = 0; t < 8; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+        mx[0] = mx[1] = -INFINITY;
+        ls[0] = ls[1] = 0.f;
+        for (int c = 0; c < un.nch; c++, kout++) {
+            const int s = kout % kBlkStages, np = min(kBlkChunk, un.p1 - (un.p0 + c * kBlkChunk));
+            const uint32_t bar = smem_addr(&full[s]), par = (uint32_t)((kout / kBlkStages) & 1);
+            uint32_t done = 0;
+            for (long long it = 0; ok && !done; it++) {
+                asm volatile(
+                    "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, "
+                    "0, p;\n}\n"
+                    : "=r"(done)
+                    : "r"(bar), "r"(par)
+                    : "memory");
+                if (!done && it > kBlkWaitLimit) ok = false;
+            }
+            // one decision for the whole CTA, so every thread meets the same barriers
+            if (__syncthreads_or(!ok)) {
+                ok = false;
+                break;
+            }
+            unsigned char* st = ring + s * kBlkStageBytes;
+            const uint32_t sk = smem_addr(st), sv = smem_addr(st + 2 * kBlkBox);
+            const bool zero_tail = np < kBlkChunk && pw + 16 > np;
+            if (zero_tail) {
+                // V rows past the block's end may hold anything: zero this
+                // warp's (P is zero there, and 0 x inf would not be)
+                for (int r = max(pw, np) + (lane >> 4); r < pw + 16; r += 2) {
+                    uint4* z = reinterpret_cast<uint4*>(st + 2 * kBlkBox + ((lane >> 3) & 1) * kBlkBox + r * 128) +
+                               (lane & 7);
+                    *z = make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+            }
+            if (pw < np) {
+                float sc[4] = {0.f, 0.f, 0.f, 0.f};  // S^T [16 positions x 8 columns]
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    // A = K rows pw.., dims 16t..: sub-matrix j = lane / 8 -> (+8 rows if j odd, +8 dims if j >= 2)
+                    const int r = pw + (lane & 7) + ((lane >> 3) & 1) * 8, d = 16 * t + (lane >> 4) * 8;
+                    uint32_t a[4];
+                    ldsm_x4(sk + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
+                    mma16816(sc, a, qb[t][0], qb[t][1]);
+                }
+                const int pa = pw + (lane >> 2), pb = pa + 8;
+#pragma unroll
+                for (int i = 0; i < 4; i++) sc[i] = (i < 2 ? pa : pb) < np ? sc[i] * scale : -INFINITY;
+                float corr[2], pr[4];
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float cm = fmaxf(sc[j], sc[j + 2]);
+                    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+                    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+                    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+                    const float mn = fmaxf(mx[j], cm);
+                    const bool none = mn == -INFINITY;
+                    corr[j] = none ? 1.f : expf(mx[j] - mn);
+                    pr[j] = none ? 0.f : expf(sc[j] - mn);
+                    pr[j + 2] = none ? 0.f : expf(sc[j + 2] - mn);
+                    float rs = pr[j] + pr[j + 2];
+                    rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+                    rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+                    rs += __shfl_xor_sync(0xffffffffu, rs, 16);
+                    ls[j] = ls[j] * corr[j] + rs;
+                    mx[j] = mn;
+                }
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    o[t][0] *= corr[0];
+                    o[t][1] *= corr[1];
+                    o[t][2] *= corr[0];
+                    o[t][3] *= corr[1];
+                }
+                // P^T as the B operand: rows (positions) 0-7 and 8-15 transposed
+                const uint32_t pb0 = movm_t(pack_h2(pr[0], pr[1])), pb1 = movm_t(pack_h2(pr[2], pr[3]));
+#pragma unroll
+                for (int t = 0; t < 8; t++) {
+                    // A = V^T dims 16t.., positions pw..: sub-matrix j -> (+8 dims if j odd, +8 rows if j >= 2)
+                    const int r = pw + (lane & 7) + (lane >> 4) * 8, d = 16 * t + ((lane >> 3) & 1) * 8;
+                    uint32_t a[4];
+                    ldsm_x4_t(sv + (d >> 6) * kBlkBox + sw128(r, (d & 63) >> 3), a);
+                    mma16816(o[t], a, pb0, pb1);
+                }
+            }
+            // every warp is done with stage s (and, after a zeroing, the
+            // generic-proxy writes are ordered before the next TMA into it)
+            if (zero_tail) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+            if (threadIdx.x == 0) issue_next();
+        }
+        if (!ok) break;
+        // merge the four warps' states of this unit and write its partial slot
+        {
+            const int j0 = 2 * (lane & 3);
+            if (lane < 4) {
+                mg_m[warp][j0] = mx[0];
+                mg_m[warp][j0 + 1] = mx[1];
+                mg_l[warp][j0] = ls[0];
+                mg_l[warp][j0 + 1] = ls[1];
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const int d = 16 * t + (lane >> 2);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int j = j0 + (i & 1), dd = d + (i >> 1) * 8;
+                    if (j < G) mg_o[warp][j][dd] = o[t][i];
+                }
+            }
+        }
+        __syncthreads();
+        {
+            const int d = threadIdx.x;  // one thread per head dimension
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                float Mx = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < 4; w++) Mx = fmaxf(Mx, mg_m[w][h]);
+                float lsum = 0.f, acc = 0.f;
+                if (Mx != -INFINITY) {
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        if (mg_m[w][h] == -INFINITY) continue;
+                        const float wt = expf(mg_m[w][h] - Mx);
+                        lsum = fmaf(mg_l[w][h], wt, lsum);
+                        acc = fmaf(mg_o[w][h][d], wt, acc);
+                    }
+                }
+                const size_t slot = ((size_t)un.m * nq + un.g * G + h) * nsplit + un.b;
+                part_o[slot * kHD + d] = acc;
+                if (d == 0) {
+                    part_ml[slot * 2] = Mx;
+                    part_ml[slot * 2 + 1] = lsum;
+                }
+            }
+        }
+        __syncthreads();  // the merge area is free for the next unit
     }
     if (!ok) {
         if ((threadIdx.x & 31) == 0) atomicExch(err, 1);
-        // chunks [c, c + kBlkStages) may still be landing in the ring: wait for
-        // them (again bounded) before the ring is reused or the CTA exits
+        // requested chunks [kout, kin) may still be landing in the ring: wait
+        // for them (again bounded) before the CTA exits
         if (threadIdx.x == 0) {
-            for (int cc = c; cc < min(nchunks, c + kBlkStages); cc++) {
-                const uint32_t bar = smem_addr(&full[cc % kBlkStages]), par = (uint32_t)((cc / kBlkStages) & 1);
+            for (int kk = kout; kk < kin; kk++) {
+                const uint32_t bar = smem_addr(&full[kk % kBlkStages]), par = (uint32_t)((kk / kBlkStages) & 1);
                 uint32_t done = 0;
                 for (long long it = 0; !done && it <= kBlkWaitLimit; it++)
                     asm volatile(
@@ -482,52 +603,6 @@ __global__ void __launch_bounds__(kThreads) attn_block_kernel(const __grid_const
                         : "r"(bar), "r"(par)
                         : "memory");
             }
-        }
-    }
-    __syncthreads();  // the ring is idle: reuse it for the merge of the four warps
-    float* sm_m = reinterpret_cast<float*>(ring);  // [4 warps][8 columns]
-    float* sm_l = sm_m + 32;
-    float* sm_o = sm_l + 32;                       // [4 warps][G][kHD]
-    {
-        const int j0 = 2 * (lane & 3);
-        if (lane < 4) {
-            sm_m[warp * 8 + j0] = mx[0];
-            sm_m[warp * 8 + j0 + 1] = mx[1];
-            sm_l[warp * 8 + j0] = ls[0];
-            sm_l[warp * 8 + j0 + 1] = ls[1];
-        }
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            const int d = 16 * t + (lane >> 2);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int j = j0 + (i & 1), dd = d + (i >> 1) * 8;
-                if (j < G) sm_o[(warp * G + j) * kHD + dd] = o[t][i];
-            }
-        }
-    }
-    __syncthreads();
-    const int d = threadIdx.x;  // one thread per head dimension
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < 4; w++) M = fmaxf(M, sm_m[w * 8 + h]);
-        float lsum = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < 4; w++) {
-                if (sm_m[w * 8 + h] == -INFINITY) continue;
-                const float wt = expf(sm_m[w * 8 + h] - M);
-                lsum = fmaf(sm_l[w * 8 + h], wt, lsum);
-                acc = fmaf(sm_o[(w * G + h) * kHD + d], wt, acc);
-            }
-        }
-        const size_t slot = ((size_t)m * nq + g * G + h) * nsplit + split;
-        part_o[slot * kHD + d] = acc;
-        if (d == 0) {
-            part_ml[slot * 2] = M;
-            part_ml[slot * 2 + 1] = lsum;
         }
     }
 }
@@ -543,12 +618,12 @@ extern "C" int b2_attention_blocks(float* out, uint16_t* out16, const float* q, 
     if (M <= 0) return 0;
     if (hd != kHD) return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_blocks: head_dim %d != 128", hd);
     if ((!out && !out16) || !q || !kv || !kv->pos || !work || !err || nkv <= 0 || nq % nkv != 0 ||
-        block <= 0 || block % kBlkChunk != 0 || kv->max_seq <= 0 || kv->n_seqs <= 0 ||
+        block <= 0 || block % kBlkChunk != 0 || kv->max_seq <= 0 || kv->n_seqs <= 0 || M > kBlkMaxRows ||
         (reinterpret_cast<uintptr_t>(kv->k_base) & 15) || (reinterpret_cast<uintptr_t>(kv->v_base) & 15) ||
         kv->seq_stride % kHD || kv->layer_stride % kHD)
         return b2_set_error(B2_ERR_INVALID_ARG,
-                            "b2_attention_blocks: bad arguments (block %% %d, 16-byte caches, strides %% 128)",
-                            kBlkChunk);
+                            "b2_attention_blocks: bad arguments (block %% %d, M <= %d, 16-byte caches, strides %% 128)",
+                            kBlkChunk, kBlkMaxRows);
     const int nsplit = (kv->max_seq + block - 1) / block;
     // rows of 128 dims the caches span for these rows (reads past it are zero-filled)
     const long long rows = ((long long)(kv->n_seqs - 1) * kv->seq_stride + (long long)kv->layer * kv->layer_stride +
@@ -560,16 +635,15 @@ extern "C" int b2_attention_blocks(float* out, uint16_t* out16, const float* q, 
     if (rc) return rc;
     float* part_ml = reinterpret_cast<float*>(work);
     float* part_o = part_ml + (size_t)M * nq * nsplit * 2;
-    dim3 grid(nsplit, nkv, M);
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    dim3 grid(2 * sms);  // two CTAs per SM; each walks its share of the units
     cudaStream_t st = (cudaStream_t)s;
     constexpr size_t smem = (size_t)kBlkStages * kBlkStageBytes + 1024;
-    static_assert((size_t)kBlkStages * kBlkStageBytes >= (64 + 4 * 8 * kHD) * sizeof(float),
-                  "merge scratch exceeds the ring");
     cudaError_t e = cudaSuccess;
     {  // more than the default 48 KB of dynamic shared memory: opt in once per device
         static bool set[8] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
         if (!set[dev & 7]) {
             e = cudaFuncSetAttribute(attn_block_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e == cudaSuccess)
@@ -582,14 +656,14 @@ extern "C" int b2_attention_blocks(float* out, uint16_t* out16, const float* q, 
         }
     }
     switch (nq / nkv) {
-        case 1: e = b2::launch_pdl(attn_block_kernel<1>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
-        case 2: e = b2::launch_pdl(attn_block_kernel<2>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
-        case 4: e = b2::launch_pdl(attn_block_kernel<4>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        case 1: e = b2::launch_pdl(attn_block_kernel<1>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, M, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        case 2: e = b2::launch_pdl(attn_block_kernel<2>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, M, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
+        case 4: e = b2::launch_pdl(attn_block_kernel<4>, grid, dim3(kThreads), smem, st, tk, tv, q, ldq, M, nq, nkv, *kv, block, part_ml, part_o, nsplit, err); break;
         default: return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_blocks: GQA group %d not in {1,2,4}", nq / nkv);
     }
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention_blocks: %s", cudaGetErrorString(e));
     e = b2::launch_pdl(attn_combine_kernel, dim3(nq, M), dim3(kHD), 0, st, out, reinterpret_cast<__half*>(out16), nq,
-                       (const float*)part_ml, (const float*)part_o, nsplit);
+                       (const float*)part_ml, (const float*)part_o, nsplit, (const int*)kv->pos, block, kv->max_seq);
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_attention_blocks combine: %s", cudaGetErrorString(e));
     return 0;
 }

@@ -104,10 +104,11 @@ MatmulDecoderBatch* matmul_decoder_batch_create(const char* model_dir, const Mat
     /* Attention in fixed blocks of positions streamed by bulk copies: the
      * work per CTA does not depend on the sequence lengths (B2_BATCH_BLOCK,
      * a multiple of 64; 0 keeps the per-sequence ranges above). */
-    b->attn_block = 1024;
+    b->attn_block = 512;
     const char* eb = getenv("B2_BATCH_BLOCK");
     if (eb) b->attn_block = atoi(eb);
-    if (b->attn_block < 0 || b->attn_block % 64) b->attn_block = 1024;
+    if (b->attn_block < 0 || b->attn_block % 64) b->attn_block = 512;
+    if (n_seqs > 512) b->attn_block = 0; /* b2_attention_blocks takes up to 512 rows */
     b->ws_split = b->split;
     if (b->attn_block > 0) {
         const int bs = b2_attention_blocks_split(max_seq_len, b->attn_block);
