@@ -91,6 +91,10 @@ class ClockSampler:
                                       stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi needs a moment to start: have it sampling before the timed region does
+            t_end = time.perf_counter() + 3.0
+            while not self.samples and time.perf_counter() < t_end:
+                time.sleep(0.01)
         except OSError:
             self.p = None
 
@@ -113,9 +117,10 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         win = [s for t, s in self.samples if t0 - 0.03 <= t <= t1 + 0.03]
         note = "timed region"
-        if not win:
-            win = [s for _, s in self.samples[-10:]]
-            note = "last samples before the end of the timed region"
+        if not win:  # a region shorter than the sampling period: the samples nearest to it
+            near = sorted(self.samples, key=lambda ts: min(abs(ts[0] - t0), abs(ts[0] - t1)))[:3]
+            win = [s for _, s in near]
+            note = "samples nearest to the timed region"
 
         def num(x):
             try:

@@ -45,6 +45,11 @@ constexpr int kStageBytes = 64 * 1024;
 constexpr int kHD = 128;
 constexpr int kMaxK = 3072;        // longest staged activation (hidden, q_dim, ffn)
 constexpr int kV = kMaxK / (4 * kConsumers);  // float4 groups of a staged vector per consumer thread
+// Copies of each layer-output accumulator: CTA c adds its down partial into
+// copy c % kOutCopies and readers sum the copies, so each address takes
+// G / kOutCopies atomic adds instead of G (the adds of all CTAs land on the
+// same H addresses; fewer per address finish sooner).
+constexpr int kOutCopies = 4;
 constexpr int kMaxSplit = 32;      // attention position ranges per kv head
 constexpr int kMaxGq = 2;          // q heads per kv head handled by one attention unit
 constexpr int kScCap = 1040;       // per-item scales prefetched into shared memory
@@ -64,7 +69,8 @@ constexpr int kActCap = 64;   // gate|up channels per CTA (the down partial's in
 struct Scratch {
     unsigned long long* cnt;   // [8 + 2L]: [0] CTAs finished, [1] best argmax key, [8 + l] down partials of
                                // layer l, [8 + L + l] attention + o_proj units of layer l
-    float* hacc;               // [L][2][H] layer outputs, summed from down partials (two token parities)
+    float* hacc;               // [L][2][kOutCopies][H] layer outputs, summed from down partials (two token
+                               // parities; a layer output is the sum of its copies)
     float* macc;               // [L][2][H] hidden after attention, summed from o_proj partials (fused phase)
     unsigned long long* hbuf;  // LL [L+1][H] layer inputs (row 0 unused: layer 0 reads the embedding)
     unsigned long long* hmid;  // LL [L][H] hidden after attention + residual
@@ -88,7 +94,7 @@ __host__ __device__ inline Scratch scratch_layout(void* base, int L, int H, int 
         return r;
     };
     s.cnt = reinterpret_cast<unsigned long long*>(take((size_t)(8 + 2 * L) * 8));
-    s.hacc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
+    s.hacc = reinterpret_cast<float*>(take((size_t)L * 2 * kOutCopies * H * 4));
     s.macc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
     s.hbuf = reinterpret_cast<unsigned long long*>(take((size_t)(L + 1) * H * 8));
     s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)L * H * 8));
@@ -646,13 +652,24 @@ struct Consumer {
     __device__ float* mid_acc(int l) const { return S.macc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
     __device__ int ao_units() const { return p.nkv * (geo.G / p.nkv); }
     // output of layer l (input of layer l + 1) for this step's parity
-    __device__ float* layer_out(int l) const { return S.hacc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
+    __device__ float* layer_out(int l) const {
+        return S.hacc + ((size_t)l * 2 + (tag & 1)) * kOutCopies * p.hidden;
+    }
+    // copies summed in a layer-output read (1 for the embedding row)
+    __device__ int out_copies(int l) const { return l < 0 ? 1 : kOutCopies; }
     // groups of a vector summed by other CTAs in this launch: read through L2
-    __device__ void cg_gather(const float* src, int K, float4 (&v)[kV]) const {
+    // (the sum of `copies` copies K values apart)
+    __device__ void cg_gather(const float* src, int K, float4 (&v)[kV], int copies = 1) const {
 #pragma unroll
         for (int j = 0; j < kV; j++) {
             const int q = tid + j * kConsumers;
-            if (q * 4 < K) v[j] = __ldcg(reinterpret_cast<const float4*>(src) + q);
+            if (q * 4 >= K) continue;
+            float4 a = __ldcg(reinterpret_cast<const float4*>(src) + q);
+            for (int c = 1; c < copies; c++) {
+                const float4 b = __ldcg(reinterpret_cast<const float4*>(src + (size_t)c * K) + q);
+                a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+            }
+            v[j] = a;
         }
     }
 
@@ -746,21 +763,27 @@ struct Consumer {
     }
     // residual rows of the item: LL words already validated by this CTA's
     // previous stage (so the poll ends at once), or the plain embedding row
-    __device__ bool load_res(const unsigned long long* ll, const float* plain) {
+    // plain[r0 + i] summed over `copies` copies p.hidden apart (layer outputs)
+    __device__ float plain_sum(const float* plain, int i, int copies) const {
+        float v = __ldcg(plain + r0 + i);
+        for (int c = 1; c < copies; c++) v += __ldcg(plain + (size_t)c * p.hidden + r0 + i);
+        return v;
+    }
+    __device__ bool load_res(const unsigned long long* ll, const float* plain, int copies = 1) {
         if (nrows > kResCap) return true;
         bool ok = true;
         for (int i = tid; i < nrows; i += kConsumers) {
             float v = 0.f;
             if (ll) ok = ll_wait(ll + r0 + i, v) && ok;
-            else v = __ldcg(plain + r0 + i);
+            else v = plain_sum(plain, i, copies);
             sh.res[buf][i] = v;
         }
         return ok;
     }
-    __device__ float resid(const unsigned long long* ll, const float* plain, int i) const {
+    __device__ float resid(const unsigned long long* ll, const float* plain, int i, int copies = 1) const {
         if (nrows <= kResCap) return sh.res[buf][i];
         float v = 0.f;
-        if (!ll) return __ldcg(plain + r0 + i);
+        if (!ll) return plain_sum(plain, i, copies);
         ll_wait(ll + r0 + i, v);  // validated by this CTA's previous stage
         return v;
     }
@@ -832,7 +855,7 @@ struct Consumer {
                 } else {
                     wait_counter(dn_count(it.l - 1), (unsigned long long)geo.G * tag);
                     if (stop()) return;
-                    cg_gather(layer_out(it.l - 1), H, v);
+                    cg_gather(layer_out(it.l - 1), H, v, kOutCopies);
                 }
                 settle(ok);
                 if (!stop()) stage(v, H, Lw.in_norm, perm);
@@ -841,13 +864,13 @@ struct Consumer {
             case IT_AO:
                 isc = Lw.o_s;
                 load_scales(Lw.o_s, 0);
-                if (it.g == 0) load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1));
+                if (it.g == 0) load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1), out_copies(it.l - 1));
                 attn_prologue(it);
                 break;
             case IT_O:
                 isc = Lw.o_s;
                 load_scales(Lw.o_s, 0);
-                ok = load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1));
+                ok = load_res(nullptr, it.l == 0 ? emb_row : layer_out(it.l - 1), out_copies(it.l - 1));
                 ok = attn_gather(it.l, v) && ok;
                 settle(ok);
                 if (!stop()) stage(v, geo.qd, nullptr, perm);
@@ -875,7 +898,7 @@ struct Consumer {
                 load_norm(p.final_norm, H);
                 wait_counter(dn_count(p.n_layers - 1), (unsigned long long)geo.G * tag);
                 if (stop()) return;
-                cg_gather(layer_out(p.n_layers - 1), H, v);
+                cg_gather(layer_out(p.n_layers - 1), H, v, kOutCopies);
                 if (geo.cta == 0) write_final(v);
                 settle(ok);
                 if (!stop()) stage(v, H, p.final_norm, false);  // int8 table
@@ -953,7 +976,7 @@ struct Consumer {
                     d.x *= sc.x, d.y *= sc.y, d.z *= sc.z, d.w *= sc.w;
                 }
                 if (geo.cta == 0) d.x += res4_.x, d.y += res4_.y, d.z += res4_.z, d.w += res4_.w;
-                red_add_v4(layer_out(it.l) + n, d);
+                red_add_v4(layer_out(it.l) + (size_t)(geo.cta % kOutCopies) * p.hidden + n, d);
             }
             consumer_sync();
             if (tid == 0) red_release(dn_count(it.l), 1ull);
@@ -1021,7 +1044,8 @@ struct Consumer {
         const float v = chunk_dot<WT>(n, K, [&](int r) { return buf_ + (size_t)r * rb; });
         if (tid < n) {
             const int r = c.a + tid;
-            const float y = resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0) + v * scale(isc, r - r0, 0);
+            const float y = resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0, out_copies(c.l - 1)) +
+                            v * scale(isc, r - r0, 0);
             ll_put(S.hmid + (size_t)c.l * H + r, y, tag);
         }
     }
@@ -1083,7 +1107,7 @@ struct Consumer {
         if (tid < n) {
             const int r = c.a + tid;
             float y = v * scale(isc, r - r0, 0);
-            if (c.g == 0) y += resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0);
+            if (c.g == 0) y += resid(nullptr, c.l == 0 ? emb_row : layer_out(c.l - 1), r - r0, out_copies(c.l - 1));
             atomicAdd(mid_acc(c.l) + r, y);
         }
     }
@@ -1415,26 +1439,27 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
         const int tok = p.state[B2_MK_TOKEN];
         const float* emb_row = p.state[B2_MK_USE_EMB] ? p.staged_emb : p.emb + (size_t)tok * p.hidden;
         Consumer<WT> cons{p, geo, sh, ring, xs, S, (uint32_t)(gen + 1), emb_row, tid, lane, warp};
-        {  // zero this CTA's slice of the next step's layer-output accumulators
-           // (the other parity; nothing reads it during this step)
-            float4* z = reinterpret_cast<float4*>(S.hacc);
-            const int per = p.hidden / 4;  // float4 per layer output
-            const int total = p.n_layers * per;
-            const int a = split_lo(total, geo.G, geo.cta), b = split_lo(total, geo.G, geo.cta + 1);
+        {  // zero this CTA's slice of the next step's accumulators (the other
+           // parity; nothing reads it during this step)
+            const int per = p.hidden / 4;  // float4 per vector
             const unsigned npar = (unsigned)(gen + 2) & 1u;
-            float4* zm = reinterpret_cast<float4*>(S.macc);
-            for (int i = a + tid; i < b; i += kConsumers) {
-                const size_t o = ((size_t)(i / per) * 2 + npar) * per + (i % per);
-                z[o] = make_float4(0.f, 0.f, 0.f, 0.f);
-                zm[o] = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4* z = reinterpret_cast<float4*>(S.hacc);  // [L][2][kOutCopies][per]
+            const int th = p.n_layers * kOutCopies * per;
+            for (int i = split_lo(th, geo.G, geo.cta) + tid; i < split_lo(th, geo.G, geo.cta + 1); i += kConsumers) {
+                const int l = i / (kOutCopies * per), rest = i % (kOutCopies * per);
+                z[((size_t)l * 2 + npar) * kOutCopies * per + rest] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            float4* zm = reinterpret_cast<float4*>(S.macc);  // [L][2][per]
+            const int tm = p.n_layers * per;
+            for (int i = split_lo(tm, geo.G, geo.cta) + tid; i < split_lo(tm, geo.G, geo.cta + 1); i += kConsumers)
+                zm[((size_t)(i / per) * 2 + npar) * per + (i % per)] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
         walk<WT>(p, geo, cons);
         if (!p.do_lm && geo.cta == 0 && !cons.stop()) {  // prefill-mode step: publish the final hidden
             cons.wait_counter(cons.dn_count(p.n_layers - 1), (unsigned long long)geo.G * (gen + 1));
             if (!cons.stop()) {
                 float4 v[kV];
-                cons.cg_gather(cons.layer_out(p.n_layers - 1), p.hidden, v);
+                cons.cg_gather(cons.layer_out(p.n_layers - 1), p.hidden, v, kOutCopies);
                 cons.write_final(v);
             }
         }
