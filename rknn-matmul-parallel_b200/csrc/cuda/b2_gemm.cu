@@ -60,7 +60,11 @@ struct Layout {
     static constexpr int kB = BN * 128;
     static constexpr int kRaw = WT == B2_W_F16 ? 0 : kATiles * kBM * raw_row_bytes<WT>();
     static constexpr int kStage = kA + kB + kRaw;
-    static constexpr int kStages = (192 * 1024) / kStage > kMaxStages ? kMaxStages : (192 * 1024) / kStage;
+    // The lm_head (ARGMAX) grid runs many waves of short CTAs: half the ring
+    // lets two CTAs share an SM, so one's prologue and epilogue overlap the
+    // other's weight stream.  The other modes keep one deep ring per SM.
+    static constexpr int kBudget = (MODE == MODE_ARGMAX ? 96 : 192) * 1024;
+    static constexpr int kStages = kBudget / kStage > kMaxStages ? kMaxStages : kBudget / kStage;
     static constexpr int kCols = MODE == MODE_PAIR ? 2 * BN : BN;  // TMEM columns (a power of two >= 32)
 };
 
