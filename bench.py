@@ -497,6 +497,8 @@ def run_batched(args, world, rank, local):
     shape = mf.ModelShape()
     n_total = args.seqs
     lens = np.random.default_rng(55).integers(128, 4097, size=n_total)
+    if n_total < world:
+        raise SystemExit(f"cfg5 needs at least one sequence per GPU ({n_total} sequences, {world} GPUs)")
     mine = shard_sequences(lens, world)[rank]
     K, W = args.steps, args.warmup
     bat = bd.BatchDecoder(mdir, len(mine), "int4", max_seq_len=4096 + K + W + 8)
