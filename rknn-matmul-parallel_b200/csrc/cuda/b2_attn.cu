@@ -1,4 +1,11 @@
-// GQA attention over the FP16 KV cache (b2_attention).
+// GQA attention over the FP16 KV cache, three entry points:
+//   b2_attention / b2_attention_f16  rows of any lengths, split-KV on CUDA cores
+//                                    (decode graph path; this header);
+//   b2_attention_blocks              many sequences of different lengths:
+//                                    persistent CTAs over fixed position blocks,
+//                                    TMA ring, tensor cores (batched decode);
+//   b2_attention_prefill             causal flash attention of consecutive rows
+//                                    of one sequence (batch prefill).
 //
 // Computes what attention_f32 (src/cpu_ops.c:202-264) and, per row,
 // attention_batch_causal_f32 (:459-571) compute: for q head h the kv head is

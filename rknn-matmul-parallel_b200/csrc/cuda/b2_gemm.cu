@@ -28,6 +28,12 @@
 // finds the gate and up sums of its channel side by side.  For ARGMAX each
 // CTA reduces its 128 vocab rows to one packed (logit, index) key per token
 // and a second kernel reduces the CTAs' keys.
+//
+// When the tiles alone would leave SMs idle (few token rows), the K range of
+// a tile is split over a thread-block cluster of 2, 4 or 8 CTAs.  Each CTA
+// pushes its partial accumulator columns into the shared memory of the CTA
+// that finishes that slice of the token columns (st.shared::cluster between
+// two cluster barriers), so every epilogue sees whole sums without atomics.
 #include <cuda.h>  // CUtensorMap and its enums; the encoder is looked up at run time
 
 #include <mutex>
