@@ -12,6 +12,7 @@ host flow on a model directory in the reference's on-disk format:
   (:1606-1610);
 * `step` = matmul_decoder_step (:1430-1634): per-layer body, prefill mode when
   no logits are wanted, final norm, lm_head, seq_len++, argmax;
+* `step_head` = matmul_decoder_step_head (:1636-1742), FP32 per-head tables;
 * `prefill_batch` = matmul_decoder_prefill_batch (:1901-2065) including its
   chunking at max_batch_prefill (default 64).
 
@@ -212,9 +213,20 @@ class RefDecoder:
 
         self.emb = _read(os.path.join(model_dir, "embeddings.bin"), np.float32,
                          self.V * H).reshape(self.V, H)
-        lm_path = os.path.join(model_dir, "lm_head.bin")
-        lm = (_read(lm_path, np.float32, self.V * H).reshape(self.V, H)
-              if os.path.exists(lm_path) else self.emb)
+        # multi-head mode (src/matmul_decoder.c:878-901): FP32 tables lm_head_NN.bin
+        self.n_heads = int(cfg.get("num_lm_heads", 0))
+        self.lm_vocab = int(cfg.get("lm_head_vocab_size", 0)) or self.V
+        self.lm_heads = []
+        if self.n_heads > 1:
+            for i in range(self.n_heads):
+                self.lm_heads.append(_read(os.path.join(model_dir, f"lm_head_{i:02d}.bin"), np.float32,
+                                           self.lm_vocab * H).reshape(self.lm_vocab, H))
+            disable_npu_lm_head = True  # no single table to quantize
+            lm = self.emb
+        else:
+            lm_path = os.path.join(model_dir, "lm_head.bin")
+            lm = (_read(lm_path, np.float32, self.V * H).reshape(self.V, H)
+                  if os.path.exists(lm_path) else self.emb)
         self.lm_f16 = lm.astype(np.float16)
         self.disable_npu_lm_head = disable_npu_lm_head
         if not disable_npu_lm_head:
@@ -308,6 +320,21 @@ class RefDecoder:
         if not want_logits:
             return 0, None
         logits = self.logits_from_hidden(h)
+        return argmax(logits), logits
+
+    def step_head(self, token_id=-1, lm_head_idx=0, embedding=None):
+        """matmul_decoder_step_head (src/matmul_decoder.c:1636-1742): the layer
+        body of `step`, final norm, then the FP32 GEMV of head lm_head_idx
+        (gemv_f32_neon, :511-566) and argmax over its vocabulary."""
+        if self.n_heads <= 1:
+            return self.step(token_id, embedding)
+        if not 0 <= lm_head_idx < self.n_heads:
+            raise ValueError("invalid lm_head_idx")
+        self.step(token_id, embedding, want_logits=False)
+        normed = rms_norm(self.last_hidden, self.final_norm, self.eps)
+        logits = np.empty(self.lm_vocab, np.float32)
+        lib().ref_lm_head_f32(_p(logits), _p(normed), _p(np.ascontiguousarray(self.lm_heads[lm_head_idx])),
+                              self.lm_vocab, self.H)
         return argmax(logits), logits
 
     def prefill_batch(self, embeds):

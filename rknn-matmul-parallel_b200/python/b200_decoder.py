@@ -42,6 +42,17 @@ class MatmulDecoderStats(ctypes.Structure):
                 ("n_steps", c_int)]
 
 
+class ProjectionWeight(ctypes.Structure):
+    _fields_ = [("data", c_vp), ("scales", c_vp), ("K", c_int), ("N", c_int), ("quant_type", c_int)]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [("q_proj", ProjectionWeight), ("k_proj", ProjectionWeight), ("v_proj", ProjectionWeight),
+                ("o_proj", ProjectionWeight), ("gate_proj", ProjectionWeight), ("up_proj", ProjectionWeight),
+                ("down_proj", ProjectionWeight), ("input_norm_weight", c_vp), ("post_attn_norm_weight", c_vp),
+                ("q_norm_weight", c_vp), ("k_norm_weight", c_vp)]
+
+
 class B2GemvArgs(ctypes.Structure):
     _fields_ = [("y", c_vp), ("ldy", c_int), ("x", c_vp), ("ldx", c_int), ("M", c_int),
                 ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
@@ -198,8 +209,46 @@ class Decoder:
             raise RuntimeError(f"matmul_decoder_create failed for {model_dir}")
         self.V, self.H = cfg.vocab_size, cfg.hidden_dim
 
+    @classmethod
+    def from_weights(cls, cfg: MatmulDecoderConfig, embeddings: np.ndarray, layers: list[dict],
+                     lm_head: np.ndarray | None, quant: str = "fp16", max_seq_len: int = 4096):
+        """matmul_decoder_create_from_weights over host arrays.  Each layer dict
+        holds the seven projections as (data, scales|None) in the on-disk layout
+        and the four FP32 norm vectors."""
+        self = cls.__new__(cls)
+        keep = [np.ascontiguousarray(embeddings, np.float32)]
+        lw = (LayerWeights * len(layers))()
+        qt = QUANT[quant]
+        H, qd, kvd, F = cfg.hidden_dim, cfg.num_q_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim, cfg.ffn_dim
+        dims = {"q_proj": (H, qd), "k_proj": (H, kvd), "v_proj": (H, kvd), "o_proj": (qd, H),
+                "gate_proj": (H, F), "up_proj": (H, F), "down_proj": (F, H)}
+        for i, L in enumerate(layers):
+            for name, (K, N) in dims.items():
+                data, sc = L[name]
+                data = np.ascontiguousarray(data)
+                keep.append(data)
+                pw = getattr(lw[i], name)
+                pw.data, pw.K, pw.N, pw.quant_type = data.ctypes.data, K, N, qt
+                if sc is not None:
+                    sc = np.ascontiguousarray(sc, np.float32)
+                    keep.append(sc)
+                    pw.scales = sc.ctypes.data
+            for f in ("input_norm_weight", "post_attn_norm_weight", "q_norm_weight", "k_norm_weight"):
+                a = np.ascontiguousarray(L[f], np.float32)
+                keep.append(a)
+                setattr(lw[i], f, a.ctypes.data)
+        lm = None if lm_head is None else np.ascontiguousarray(lm_head, np.float32)
+        cfg.max_seq_len = max_seq_len
+        self.cfg = cfg
+        self.ctx = capi().matmul_decoder_create_from_weights(ctypes.byref(cfg), keep[0].ctypes.data, lw,
+                                                             _ptr(lm), qt, max_seq_len)
+        if not self.ctx:
+            raise RuntimeError("matmul_decoder_create_from_weights failed")
+        self.V, self.H = cfg.vocab_size, cfg.hidden_dim
+        return self
+
     def close(self):
-        if self.ctx:
+        if getattr(self, "ctx", None):
             capi().matmul_decoder_destroy(self.ctx)
             self.ctx = None
 
@@ -216,6 +265,15 @@ class Decoder:
         tok = self.step(token_id, embedding, logits)
         if tok < 0:
             raise RuntimeError(f"step failed ({tok})")
+        return tok, logits
+
+    def step_head(self, token_id=-1, lm_head_idx=0, embedding=None):
+        """matmul_decoder_step_head; returns (token, logits[lm_head_vocab])."""
+        n = self.cfg.lm_head_vocab_size if self.cfg.num_lm_heads > 1 and self.cfg.lm_head_vocab_size > 0 \
+            else self.V
+        logits = np.empty(n, np.float32)
+        emb = None if embedding is None else np.ascontiguousarray(embedding, np.float32)
+        tok = capi().matmul_decoder_step_head(self.ctx, token_id, _ptr(emb), lm_head_idx, logits.ctypes.data)
         return tok, logits
 
     def step_token(self, token_id=-1, embedding=None):

@@ -13,7 +13,8 @@ Behaviour differences, each fixing a reference defect:
     python/matmul_decoder.py:202, which the C step rejects);
   * the default config uses head_dim 128 (the reference writes 64, :95);
   * weights count as present with either embeddings.npy or embeddings.bin
-    (the C loader reads embeddings.bin; the reference checks only .npy, :147).
+    (the C loader reads embeddings.bin; the reference checks only .npy, :147);
+  * the result dict also carries "token_ids", the generated ids (additive key).
 """
 from __future__ import annotations
 
@@ -128,7 +129,8 @@ class MatmulDecoder:
         return {"text": text,
                 "perf": {"prefill_time_ms": (t_pre - t0) * 1e3, "generate_time_ms": (t_gen - t_pre) * 1e3,
                          "generate_tokens": len(tokens)},
-                "n_tokens_generated": len(tokens), "ret_code": 0, "aborted": False}
+                "n_tokens_generated": len(tokens), "ret_code": 0, "aborted": False,
+                "token_ids": tokens}
 
     def release(self):
         self._decoder = None

@@ -6,6 +6,7 @@ The layout is the one the reference loader reads (src/matmul_decoder.c:635-826,
     model_dir/config.json                 keys parsed by matmul_decoder_load_config
     model_dir/embeddings.bin              FP32 [vocab, hidden]
     model_dir/lm_head.bin                 FP32 [vocab, hidden] (only when untied)
+    model_dir/lm_head_NN.bin              FP32 [lm_head_vocab, hidden] per head (multi-head)
     model_dir/final_norm.bin              FP32 [hidden]
     model_dir/layers/layer_NN/input_norm.bin, post_attn_norm.bin   FP32 [hidden]
     model_dir/layers/layer_NN/q_norm.bin, k_norm.bin               FP32 [head_dim]
@@ -52,6 +53,8 @@ class ModelShape:
     has_qk_norm: int = 1
     tie_word_embeddings: bool = True
     name: str = "qwen3-0.6b-synthetic"
+    num_lm_heads: int = 0         # > 1: multi-head model (lm_head_NN.bin tables, step_head)
+    lm_head_vocab_size: int = 0   # vocabulary of each head in multi-head mode
     extra: dict = field(default_factory=dict)
 
     def proj_shapes(self):
@@ -68,6 +71,9 @@ class ModelShape:
              "rms_eps": self.rms_eps, "rope_theta": self.rope_theta,
              "rope_style": self.rope_style, "has_qk_norm": self.has_qk_norm,
              "tie_word_embeddings": bool(self.tie_word_embeddings)}
+        if self.num_lm_heads > 1:
+            d["num_lm_heads"] = self.num_lm_heads
+            d["lm_head_vocab_size"] = self.lm_head_vocab_size or self.vocab_size
         d.update(self.extra)
         return d
 
@@ -140,7 +146,12 @@ def write_synthetic_model(model_dir: str, shape: ModelShape, quant: str | None =
     synth_embeddings(shape).tofile(os.path.join(model_dir, "embeddings.bin"))
     _normal(GLOBAL_SEED["final_norm"], (shape.hidden_dim,), 0.01, 1.0).tofile(
         os.path.join(model_dir, "final_norm.bin"))
-    if not shape.tie_word_embeddings:
+    if shape.num_lm_heads > 1:  # one FP32 table per head (src/matmul_decoder.c:883-901)
+        lv = shape.lm_head_vocab_size or shape.vocab_size
+        for i in range(shape.num_lm_heads):
+            _normal(GLOBAL_SEED["lm_head"] + 1 + i, (lv, shape.hidden_dim), 0.02).tofile(
+                os.path.join(model_dir, f"lm_head_{i:02d}.bin"))
+    elif not shape.tie_word_embeddings:
         _normal(GLOBAL_SEED["lm_head"], (shape.vocab_size, shape.hidden_dim), 0.02).tofile(
             os.path.join(model_dir, "lm_head.bin"))
     for layer in range(shape.num_layers):
