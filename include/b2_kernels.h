@@ -292,6 +292,14 @@ typedef struct {
                               (FP16 / int8, or int4 [ffn][hidden/2] with
                               the even output column in the low nibble);
                               scales are dn_s                               */
+    /* Tile-major copies read by b2_mk2_decode (b2_tile_relayout of the row
+     * arrays above): 16-row tiles, each stored as [64-byte super-block][16
+     * rows][64 bytes], so one tile is one contiguous block whose shared-memory
+     * image the tensor-core row dots read without bank conflicts. */
+    const void* qkv_t;     /* tiles of the qkv rows                         */
+    const void* o_t;       /* tiles of the o rows                           */
+    const void* gu_t;      /* tiles of 8 channels: rows gate(c), up(c), ... */
+    const float* gu_ts;    /* per-row scales of gu_t (interleaved), or NULL */
 } B2MkLayer;
 
 typedef struct {
@@ -315,6 +323,11 @@ typedef struct {
     void* scratch;             /* b2_mk_scratch_bytes() bytes, zeroed once    */
     const B2MkLayer* layers;   /* device array [n_layers] (kept off the kernel
                                   parameter block, which stays small)         */
+    const void* lm_t;          /* tile-major int8 lm_head (b2_mk2_decode)      */
+    long long poll_limit;      /* polls before a wait gives up (0: default)   */
+    int stall_test;            /* 1: the lm_head phase waits for a flag value
+                                  that never comes (tests the timed-out-wait
+                                  path of b2_mk2_decode)                      */
 } B2MkPlan;
 
 /* 0 when the plan's shapes are supported by the persistent kernel. */
@@ -326,6 +339,30 @@ int b2_mk_decode(const B2MkPlan* plan, b2_stream_t s);
 float* b2_mk_final_hidden(const B2MkPlan* plan);
 /* Dynamic shared memory of one CTA of the persistent kernel. */
 size_t b2_mk_smem_bytes(void);
+
+/* Second-generation persistent decode kernel (same plan, same state block
+ * layout; give it its own state block and scratch).  One producer thread per
+ * CTA turns the CTA's share of the token into a stream of operations in
+ * shared memory: data operations carry a block of tile-major weight rows (or
+ * K/V positions) copied in by bulk copies, control operations stage the input
+ * of the next phase.  The consumer warps take the stream in order and split
+ * every 16-row tile's dot products over their K ranges.  Attention and o_proj
+ * run fused per (kv head, row slice) unit; the host routes contexts up to
+ * b2_mk2_max_context() cached positions here. */
+int b2_mk2_check(const B2MkPlan* plan);
+int b2_mk2_max_context(void);
+size_t b2_mk2_scratch_bytes(int n_layers, int hidden, int ffn, int nq, int nkv, int hd);
+int b2_mk2_decode(const B2MkPlan* plan, b2_stream_t s);
+float* b2_mk2_final_hidden(const B2MkPlan* plan);
+
+/* Tile-major relayout (one-time, at load): dst gets rows [0, rows) of the
+ * row-major src (row_bytes per row; rows % 16 == 0, row_bytes % 64 == 0) as
+ * 16-row tiles [row_bytes/64][16][64 bytes].  pair_half > 0 interleaves two
+ * halves of src: tile t row 2j is src row 8t + j and row 2j+1 is src row
+ * pair_half + 8t + j (gate and up of one channel).  When src_s is non-NULL,
+ * dst_s[r] = src_s[source row of r]. */
+int b2_tile_relayout(void* dst, const void* src, int rows, int row_bytes, int pair_half, float* dst_s,
+                     const float* src_s, b2_stream_t s);
 
 #ifdef __cplusplus
 }

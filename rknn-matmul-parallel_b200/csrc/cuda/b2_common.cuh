@@ -164,8 +164,12 @@ __host__ __device__ constexpr float x_scale() {
 }
 
 // Orderable encoding of a float: a larger float maps to a larger unsigned.
+// NaN maps to 0, below every number: the reference argmax's strict '>' scan
+// never moves to a NaN after its first element (src/cpu_ops.c:575-586).
+// (It differs only when element 0 itself is NaN: the scan then returns 0.)
 __device__ __forceinline__ uint32_t float_order(float f) {
     uint32_t u = __float_as_uint(f);
+    if (f != f) return 0u;
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

@@ -59,12 +59,20 @@ struct MatmulDecoderContext {
     b2_graph_t g_head, g_nohead, g_loop;
     int use_mk;       /* persistent decode kernel selected */
     int mk_max_ctx;   /* ... for steps below this many cached positions */
-    int hidden_mk;    /* last token's hidden lives in the persistent kernel's scratch */
+    int hidden_mk;    /* last token's hidden lives in a persistent kernel's scratch (1: first, 2: second) */
     B2MkPlan mk;
     B2MkLayer* d_mk_layers; /* device copy of the per-layer pointer table */
     int* d_mk_state;  /* B2_MK_STATE_INTS */
     int* h_mk_state;  /* pinned mirror */
     void* mk_scratch;
+    /* second-generation persistent kernel: its own plan, state block and scratch */
+    int use_mk2;
+    B2MkPlan mk2;
+    B2MkLayer* d_mk2_layers;
+    int* d_mk2_state;
+    int* h_mk2_state;
+    void* mk2_buf;    /* tile-major weights, lm_head tiles, scratch and state (one allocation) */
+    size_t mk2_scratch_bytes;
     b2_event_t ev[3];
     MatmulDecoderStats stats;
 };
@@ -239,6 +247,82 @@ static void mk_setup(MatmulDecoderContext* ctx) {
     ctx->mk_max_ctx = mx && atoi(mx) > 0 ? atoi(mx) : MD_MK_MAX_CONTEXT;
 }
 
+/* The second-generation persistent kernel: tile-major copies of the layer
+ * weights and of the INT8 lm_head (b2_tile_relayout), its own state block and
+ * scratch, in one device allocation.  Selected when the first plan is valid
+ * and the shapes fit (B2_DECODE_KERNEL=mk1 keeps the first kernel). */
+static void mk2_setup(MatmulDecoderContext* ctx) {
+    const char* env = getenv("B2_DECODE_KERNEL");
+    if (!ctx->use_mk || (env && (strcmp(env, "mk1") == 0 || strcmp(env, "graph") == 0))) return;
+    DevModel* m = &ctx->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    B2MkPlan* p = &ctx->mk2;
+    *p = ctx->mk;
+    const int L = c->num_layers, H = c->hidden_dim, F = c->ffn_dim;
+    const int qd = c->num_q_heads * c->head_dim, nqkv = qd + 2 * c->num_kv_heads * c->head_dim;
+    const int wt = m->wtype;
+    const size_t rb_h = wt == B2_W_F16 ? (size_t)H * 2 : wt == B2_W_I8 ? (size_t)H : (size_t)H / 2;
+    const size_t rb_o = wt == B2_W_F16 ? (size_t)qd * 2 : wt == B2_W_I8 ? (size_t)qd : (size_t)qd / 2;
+#define MK2_AL(x) (((x) + 255) & ~(size_t)255)
+    const size_t per_layer = MK2_AL((size_t)nqkv * rb_h) + MK2_AL((size_t)H * rb_o) + MK2_AL((size_t)2 * F * rb_h) +
+                             MK2_AL((size_t)2 * F * 4);
+    const size_t lm_bytes = MK2_AL((size_t)c->vocab_size * H);
+    ctx->mk2_scratch_bytes = MK2_AL(b2_mk2_scratch_bytes(L, H, F, c->num_q_heads, c->num_kv_heads, c->head_dim));
+    const size_t total = per_layer * L + lm_bytes + ctx->mk2_scratch_bytes + MK2_AL(sizeof(B2MkLayer) * L) +
+                         MK2_AL(B2_MK_STATE_INTS * 4);
+    unsigned char* base = NULL;
+    if (b2_malloc((void**)&base, total)) {
+        MD_LOG("second persistent kernel disabled: %s\n", b2_last_error());
+        return;
+    }
+    ctx->mk2_buf = base;
+    size_t off = 0;
+#define MK2_TAKE(n) (off += MK2_AL(n), base + off - MK2_AL(n))
+    B2MkLayer* table = (B2MkLayer*)calloc((size_t)L, sizeof(B2MkLayer));
+    int rc = table ? b2_memcpy_d2h(table, ctx->d_mk_layers, sizeof(B2MkLayer) * (size_t)L, NULL) : -1;
+    if (!rc) rc = b2_stream_sync(NULL);
+    for (int l = 0; l < L && !rc; l++) {
+        const DevLayer* D = &m->layers[l];
+        void* qkv_t = MK2_TAKE((size_t)nqkv * rb_h);
+        void* o_t = MK2_TAKE((size_t)H * rb_o);
+        void* gu_t = MK2_TAKE((size_t)2 * F * rb_h);
+        float* gu_ts = (float*)MK2_TAKE((size_t)2 * F * 4);
+        rc = b2_tile_relayout(qkv_t, D->qkv.w, nqkv, (int)rb_h, 0, NULL, NULL, NULL);
+        if (!rc) rc = b2_tile_relayout(o_t, D->o.w, H, (int)rb_o, 0, NULL, NULL, NULL);
+        if (!rc) rc = b2_tile_relayout(gu_t, D->gu.w, 2 * F, (int)rb_h, F, D->gu.s ? gu_ts : NULL, D->gu.s, NULL);
+        table[l].qkv_t = qkv_t;
+        table[l].o_t = o_t;
+        table[l].gu_t = gu_t;
+        table[l].gu_ts = D->gu.s ? gu_ts : NULL;
+    }
+    void* lm_t = MK2_TAKE((size_t)c->vocab_size * H);
+    if (!rc) rc = b2_tile_relayout(lm_t, m->lm, c->vocab_size, H, 0, NULL, NULL, NULL);
+    p->scratch = MK2_TAKE(ctx->mk2_scratch_bytes);
+    ctx->d_mk2_layers = (B2MkLayer*)MK2_TAKE(sizeof(B2MkLayer) * L);
+    ctx->d_mk2_state = (int*)MK2_TAKE(B2_MK_STATE_INTS * 4);
+#undef MK2_TAKE
+#undef MK2_AL
+    if (!rc) rc = b2_memcpy_h2d(ctx->d_mk2_layers, table, sizeof(B2MkLayer) * (size_t)L, NULL);
+    if (!rc) rc = b2_memset(p->scratch, 0, ctx->mk2_scratch_bytes, NULL);
+    if (!rc) rc = b2_memset(ctx->d_mk2_state, 0, B2_MK_STATE_INTS * 4, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    if (!rc) rc = b2_host_alloc((void**)&ctx->h_mk2_state, B2_MK_STATE_INTS * 4);
+    free(table);
+    p->layers = ctx->d_mk2_layers;
+    p->lm_t = lm_t;
+    p->state = ctx->d_mk2_state;
+    {
+        /* test-only: a short poll limit, and a wait that never completes, for
+         * the tests of the timed-out-wait path */
+        const char* pl = getenv("B2_MK_POLL_LIMIT");
+        p->poll_limit = pl && atoll(pl) > 0 ? atoll(pl) : 0;
+        const char* st = getenv("B2_MK_STALL_TEST");
+        p->stall_test = st && atoi(st) > 0 ? 1 : 0;
+    }
+    ctx->use_mk2 = !rc && b2_mk2_check(p) == 0;
+    if (rc) MD_LOG("second persistent kernel disabled (%d): %s\n", rc, b2_last_error());
+}
+
 static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {
     int rc = ctx_alloc(ctx);
     if (rc) {
@@ -247,12 +331,14 @@ static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {
         return NULL;
     }
     mk_setup(ctx);
+    mk2_setup(ctx);
     ctx->config = ctx->model.cfg;
     printf("[MatmulDecoder] Ready: %d layers, hidden=%d, heads=%d/%d, ffn=%d, vocab=%d, quant=%d, "
            "max_seq=%d, arena %.1f MB, decode kernel: %s\n",
            ctx->config.num_layers, ctx->config.hidden_dim, ctx->config.num_q_heads,
            ctx->config.num_kv_heads, ctx->config.ffn_dim, ctx->config.vocab_size, ctx->model.quant,
-           ctx->max_seq, ctx->model.arena.size / 1e6, ctx->use_mk ? "persistent" : "graph");
+           ctx->max_seq, ctx->model.arena.size / 1e6,
+           ctx->use_mk2 ? "persistent (tile stream below 512 cached positions)" : ctx->use_mk ? "persistent" : "graph");
     return ctx;
 }
 
@@ -340,6 +426,8 @@ void matmul_decoder_destroy(MatmulDecoderContext* ctx) {
     b2_host_free(ctx->h_pos);
     b2_host_free(ctx->h_loop);
     b2_host_free(ctx->h_mk_state);
+    b2_host_free(ctx->h_mk2_state);
+    if (ctx->mk2_buf) b2_free(ctx->mk2_buf);
     md_model_free(&ctx->model);
     free(ctx);
 }
@@ -433,42 +521,63 @@ static void record_stats(MatmulDecoderContext* ctx, double t0, double t_copy, in
     ctx->stats.n_steps++;
 }
 
-/* A persistent-kernel wait timed out: clear its counters and generation so the
- * next step starts from a consistent state, and report a runtime error. */
-static int mk_recover(MatmulDecoderContext* ctx, int code) {
+/* Which persistent kernel runs tokens at positions [pos, pos + n): 2 = the
+ * tile-stream kernel, 1 = the first kernel, 0 = none (graph of per-op kernels). */
+static int mk_kind(const MatmulDecoderContext* ctx, int pos, int n) {
+    if (ctx->use_mk2 && pos + n <= b2_mk2_max_context()) return 2;
+    if (ctx->use_mk && pos + n <= ctx->mk_max_ctx) return 1;
+    return 0;
+}
+
+static B2MkPlan* mk_plan(MatmulDecoderContext* ctx, int kind) { return kind == 2 ? &ctx->mk2 : &ctx->mk; }
+static int* mk_dstate(MatmulDecoderContext* ctx, int kind) { return kind == 2 ? ctx->d_mk2_state : ctx->d_mk_state; }
+static int* mk_hstate(MatmulDecoderContext* ctx, int kind) { return kind == 2 ? ctx->h_mk2_state : ctx->h_mk_state; }
+static int mk_launch(MatmulDecoderContext* ctx, int kind) {
+    return kind == 2 ? b2_mk2_decode(&ctx->mk2, ctx->stream) : b2_mk_decode(&ctx->mk, ctx->stream);
+}
+
+/* A persistent-kernel wait timed out: clear its scratch (counters, flags,
+ * accumulators) and state block so the next step starts from a consistent
+ * state, and report a runtime error. */
+static int mk_recover(MatmulDecoderContext* ctx, int kind, int code) {
     MD_LOG("persistent decode kernel reported error %d (timed-out wait); state reset\n", code);
     const MatmulDecoderConfig* c = &ctx->model.cfg;
-    const size_t bytes = b2_mk_scratch_bytes(c->num_layers, c->hidden_dim, c->ffn_dim, c->num_q_heads,
-                                             c->num_kv_heads, c->head_dim);
-    b2_memset(ctx->mk_scratch, 0, bytes, ctx->stream);
-    b2_memset(ctx->d_mk_state, 0, B2_MK_STATE_INTS * 4, ctx->stream);
+    if (kind == 2) {
+        b2_memset(ctx->mk2.scratch, 0, ctx->mk2_scratch_bytes, ctx->stream);
+    } else {
+        const size_t bytes = b2_mk_scratch_bytes(c->num_layers, c->hidden_dim, c->ffn_dim, c->num_q_heads,
+                                                 c->num_kv_heads, c->head_dim);
+        b2_memset(ctx->mk_scratch, 0, bytes, ctx->stream);
+    }
+    b2_memset(mk_dstate(ctx, kind), 0, B2_MK_STATE_INTS * 4, ctx->stream);
     b2_stream_sync(ctx->stream);
     return MATMUL_DECODER_ERR_RKNN;
 }
 
-static int mk_step(MatmulDecoderContext* ctx, int token_id, const float* embedding, int with_head,
+static int mk_step(MatmulDecoderContext* ctx, int kind, int token_id, const float* embedding, int with_head,
                    float* logits_out) {
     const double t0 = now_ms();
     const int H = ctx->model.cfg.hidden_dim;
-    int* st = ctx->h_mk_state;
+    int* st = mk_hstate(ctx, kind);
+    int* dst = mk_dstate(ctx, kind);
     st[B2_MK_TOKEN] = embedding ? 0 : token_id;
     st[B2_MK_POS] = ctx->seq_len;
     st[B2_MK_STEP] = 0;
     st[B2_MK_USE_EMB] = embedding ? 1 : 0;
     b2_stream_t s = ctx->stream;
-    int rc = b2_memcpy_h2d(ctx->d_mk_state, st, 4 * 4, s);
+    int rc = b2_memcpy_h2d(dst, st, 4 * 4, s);
     if (!rc && embedding) {
         memcpy(ctx->h_blk + PARAMS_INTS, embedding, (size_t)H * 4);
         rc = b2_memcpy_h2d(ctx->d_blk + PARAMS_INTS, ctx->h_blk + PARAMS_INTS, (size_t)H * 4, s);
     }
-    ctx->mk.do_lm = with_head;
+    mk_plan(ctx, kind)->do_lm = with_head;
     if (!rc) rc = b2_event_record(ctx->ev[0], s);
-    if (!rc) rc = b2_mk_decode(&ctx->mk, s);
+    if (!rc) rc = mk_launch(ctx, kind);
     if (!rc) rc = b2_event_record(ctx->ev[2], s);
-    if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, ctx->d_mk_state + B2_MK_ERR, 2 * 4, s);
+    if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, dst + B2_MK_ERR, 2 * 4, s);
     if (!rc) rc = b2_stream_sync(s);
     if (rc) return fail("persistent decode step", rc);
-    if (st[B2_MK_ERR]) return mk_recover(ctx, st[B2_MK_ERR]);
+    if (st[B2_MK_ERR]) return mk_recover(ctx, kind, st[B2_MK_ERR]);
     double t_copy = 0;
     if (with_head && logits_out) {
         const double tc = now_ms();
@@ -478,7 +587,7 @@ static int mk_step(MatmulDecoderContext* ctx, int token_id, const float* embeddi
         t_copy = now_ms() - tc;
     }
     ctx->seq_len++;
-    ctx->hidden_mk = 1;
+    ctx->hidden_mk = kind;
     float ms = 0.f;
     b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[2]);
     ctx->stats.total_ms = (float)(now_ms() - t0);
@@ -497,7 +606,8 @@ static int step_impl(MatmulDecoderContext* ctx, int token_id, const float* embed
     int rc = check_step_args(ctx, token_id, embedding, ctx ? ctx->model.cfg.vocab_size : 0);
     if (rc) return rc;
     b2_set_device(ctx->device);
-    if (ctx->use_mk && ctx->seq_len < ctx->mk_max_ctx) return mk_step(ctx, token_id, embedding, with_head, logits_out);
+    const int kind = mk_kind(ctx, ctx->seq_len, 1);
+    if (kind) return mk_step(ctx, kind, token_id, embedding, with_head, logits_out);
     const double t0 = now_ms();
     b2_graph_t* g = with_head ? &ctx->g_head : &ctx->g_nohead;
     if (!*g && (rc = build_graph(ctx, with_head, g))) return fail("graph capture", rc);
@@ -604,27 +714,29 @@ int matmul_decoder_decode_greedy(MatmulDecoderContext* ctx, int first_token, int
     const double t0 = now_ms();
     b2_set_device(ctx->device);
     int rc = 0;
-    if (ctx->use_mk && ctx->seq_len + n_tokens <= ctx->mk_max_ctx) {
-        int* st = ctx->h_mk_state;
+    const int kind = mk_kind(ctx, ctx->seq_len, n_tokens);
+    if (kind) {
+        int* st = mk_hstate(ctx, kind);
+        int* dst = mk_dstate(ctx, kind);
         st[B2_MK_TOKEN] = first_token;
         st[B2_MK_POS] = ctx->seq_len;
         st[B2_MK_STEP] = 0;
         st[B2_MK_USE_EMB] = 0;
-        ctx->mk.do_lm = 1;
-        rc = b2_memcpy_h2d(ctx->d_mk_state, st, 4 * 4, ctx->stream);
+        mk_plan(ctx, kind)->do_lm = 1;
+        rc = b2_memcpy_h2d(dst, st, 4 * 4, ctx->stream);
         if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
-        for (int i = 0; i < n_tokens && !rc; i++) rc = b2_mk_decode(&ctx->mk, ctx->stream);
+        for (int i = 0; i < n_tokens && !rc; i++) rc = mk_launch(ctx, kind);
         if (!rc) rc = b2_event_record(ctx->ev[2], ctx->stream);
         if (!rc) rc = b2_memcpy_d2h(tokens_out, ctx->d_hist, (size_t)n_tokens * 4, ctx->stream);
-        if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, ctx->d_mk_state + B2_MK_ERR, 4, ctx->stream);
+        if (!rc) rc = b2_memcpy_d2h(st + B2_MK_ERR, dst + B2_MK_ERR, 4, ctx->stream);
         if (!rc) rc = b2_stream_sync(ctx->stream);
         if (rc) return fail("decode_greedy", rc);
-        if (st[B2_MK_ERR]) return mk_recover(ctx, st[B2_MK_ERR]);
+        if (st[B2_MK_ERR]) return mk_recover(ctx, kind, st[B2_MK_ERR]);
         float ms = 0.f;
         b2_event_elapsed_ms(&ms, ctx->ev[0], ctx->ev[2]);
         if (device_ms) *device_ms = ms;
         ctx->seq_len += n_tokens;
-        ctx->hidden_mk = 1;
+        ctx->hidden_mk = kind;
         ctx->stats.total_ms = (float)(now_ms() - t0);
         ctx->stats.matmul_ms = ms;
         ctx->stats.lm_head_ms = 0.f;
@@ -728,7 +840,9 @@ int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out) {
     if (!ctx || !hidden_out) return MATMUL_DECODER_ERR_INVALID_ARG;
     b2_set_device(ctx->device);
     const size_t H = (size_t)ctx->model.cfg.hidden_dim;
-    const float* src = ctx->hidden_mk ? b2_mk_final_hidden(&ctx->mk) : ctx->hidden + (size_t)ctx->hidden_row * H;
+    const float* src = ctx->hidden_mk == 2   ? b2_mk2_final_hidden(&ctx->mk2)
+                       : ctx->hidden_mk == 1 ? b2_mk_final_hidden(&ctx->mk)
+                                             : ctx->hidden + (size_t)ctx->hidden_row * H;
     int rc = b2_memcpy_d2h(hidden_out, src, H * 4, ctx->stream);
     if (!rc) rc = b2_stream_sync(ctx->stream);
     return rc ? fail("get_hidden", rc) : MATMUL_DECODER_OK;

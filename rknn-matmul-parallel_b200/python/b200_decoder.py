@@ -161,6 +161,12 @@ SIGNATURES = {
     "b2_mk_decode": (c_int, [c_vp, c_vp]),
     "b2_mk_final_hidden": (c_vp, [c_vp]),
     "b2_mk_smem_bytes": (c_size, []),
+    "b2_mk2_check": (c_int, [c_vp]),
+    "b2_mk2_max_context": (c_int, []),
+    "b2_mk2_scratch_bytes": (c_size, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "b2_mk2_decode": (c_int, [c_vp, c_vp]),
+    "b2_mk2_final_hidden": (c_vp, [c_vp]),
+    "b2_tile_relayout": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     "b2_lm_head_argmax": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_float,
                                   c_vp, c_int, c_vp, c_vp, c_vp]),
 }
