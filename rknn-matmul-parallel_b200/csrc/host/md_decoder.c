@@ -72,6 +72,7 @@ struct MatmulDecoderContext {
     int* d_mk2_state;
     int* h_mk2_state;
     void* mk2_buf;    /* tile-major weights, lm_head tiles, scratch and state (one allocation) */
+    int test_hooks;   /* B2_MK_POLL_LIMIT was set at create: B2_MK_STALL_TEST is read per step */
     size_t mk2_scratch_bytes;
     b2_event_t ev[3];
     MatmulDecoderStats stats;
@@ -316,8 +317,8 @@ static void mk2_setup(MatmulDecoderContext* ctx) {
          * the tests of the timed-out-wait path */
         const char* pl = getenv("B2_MK_POLL_LIMIT");
         p->poll_limit = pl && atoll(pl) > 0 ? atoll(pl) : 0;
-        const char* st = getenv("B2_MK_STALL_TEST");
-        p->stall_test = st && atoi(st) > 0 ? 1 : 0;
+        ctx->test_hooks = p->poll_limit > 0;
+        p->stall_test = 0;
     }
     ctx->use_mk2 = !rc && b2_mk2_check(p) == 0;
     if (rc) MD_LOG("second persistent kernel disabled (%d): %s\n", rc, b2_last_error());
@@ -571,6 +572,10 @@ static int mk_step(MatmulDecoderContext* ctx, int kind, int token_id, const floa
         rc = b2_memcpy_h2d(ctx->d_blk + PARAMS_INTS, ctx->h_blk + PARAMS_INTS, (size_t)H * 4, s);
     }
     mk_plan(ctx, kind)->do_lm = with_head;
+    if (ctx->test_hooks) {
+        const char* stall = getenv("B2_MK_STALL_TEST");
+        ctx->mk2.stall_test = stall && atoi(stall) > 0;
+    }
     if (!rc) rc = b2_event_record(ctx->ev[0], s);
     if (!rc) rc = mk_launch(ctx, kind);
     if (!rc) rc = b2_event_record(ctx->ev[2], s);
@@ -723,6 +728,10 @@ int matmul_decoder_decode_greedy(MatmulDecoderContext* ctx, int first_token, int
         st[B2_MK_STEP] = 0;
         st[B2_MK_USE_EMB] = 0;
         mk_plan(ctx, kind)->do_lm = 1;
+        if (ctx->test_hooks) {
+            const char* stall = getenv("B2_MK_STALL_TEST");
+            ctx->mk2.stall_test = stall && atoi(stall) > 0;
+        }
         rc = b2_memcpy_h2d(dst, st, 4 * 4, ctx->stream);
         if (!rc) rc = b2_event_record(ctx->ev[0], ctx->stream);
         for (int i = 0; i < n_tokens && !rc; i++) rc = mk_launch(ctx, kind);
