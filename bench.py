@@ -569,6 +569,12 @@ def run_batched(args, world, rank, local, sub=False):
     mine = shard_sequences(lens, world)[rank]
     K, W = args.steps, args.warmup
     bat = bd.BatchDecoder(mdir, len(mine), "int4", max_seq_len=4096 + K + W + 8)
+    sharded = world > 1 and os.environ.get("B2_SHARD_VOCAB", "1") != "0"
+    if sharded:  # each rank keeps 1/world of the lm_head; NCCL all-gather + all-reduce MAX per step
+        import torch.distributed as dist
+        obj = [bd.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        bat.shard_vocab(rank, world, obj[0], max(len(p) for p in shard_sequences(lens, world)))
 
     def reset():
         for i, s in enumerate(mine):
@@ -597,9 +603,10 @@ def run_batched(args, world, rank, local, sub=False):
     my_lens = [int(lens[s]) for s in mine]
     attended = float(np.mean(my_lens)) + (K + 1) / 2.0
     kv_bytes = len(mine) * shape.num_layers * 2 * shape.num_kv_heads * shape.head_dim * 2 * attended
-    bytes_step = layer_weight_bytes(shape, "int4") + shape.vocab_size * (shape.hidden_dim + 4) + kv_bytes
     kv_max = max_over_ranks(world, kv_bytes)  # the rank with the most KV bytes sets the step time
-    bytes_step_max = layer_weight_bytes(shape, "int4") + shape.vocab_size * (shape.hidden_dim + 4) + kv_max
+    lm_bytes = shape.vocab_size * (shape.hidden_dim + 4) / (world if sharded else 1)
+    bytes_step = layer_weight_bytes(shape, "int4") + lm_bytes + kv_bytes
+    bytes_step_max = layer_weight_bytes(shape, "int4") + lm_bytes + kv_max
     peaks = load_peaks()
     peak = float(peaks.get("hbm_gbs", 6650.0))
     achieved = bytes_step_max / (dev_s / K) / 1e9
@@ -619,6 +626,8 @@ def run_batched(args, world, rank, local, sub=False):
                 "n_gpus": world, "value": round(n_total * K / dev_s, 2), "unit": "tok/s",
                 "ms_per_step": round(dev_s * 1e3 / K, 3), "scaling": "strong",
                 "e2e": round(n_total * K / dt, 2), "roofline": roof, "clocks": clk,
+                "lm_head": f"vocab-sharded over {world} ranks (NCCL all-gather + all-reduce MAX)" if sharded
+                           else "replicated",
                 "note": "all 64 sequences advance one greedy token per step; device time is the max over ranks",
                 "_launches": launches_per_step * K}
     cpu = None
@@ -634,7 +643,8 @@ def run_batched(args, world, rank, local, sub=False):
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights / fp16 act",
             "data": "synthetic; KV contents zero (attention cost is value-independent)",
             "config": {"workload": "cfg5", "sequences": n_total, "per_gpu": len(mine), "context": "U[128,4096]",
-                       "parallelism": f"sequences sharded over {world} GPUs",
+                       "parallelism": f"sequences sharded over {world} GPUs"
+                                      + (", lm_head vocab-sharded (NCCL)" if sharded else ""),
                        "l2": "inputs larger than L2: %.2f GB of weights and KV per step per GPU" % (bytes_step / 1e9)},
             "roofline": roof,
             "clocks": clk,

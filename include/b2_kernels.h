@@ -70,6 +70,9 @@ int b2_memset(void* dst, int value, size_t bytes, b2_stream_t s);
 int b2_stream_create(b2_stream_t* s);
 int b2_stream_destroy(b2_stream_t s);
 int b2_stream_sync(b2_stream_t s);
+/* 0 when all work of the stream has completed, 1 while some is pending,
+ * negative on an error (lets a caller bound its wait). */
+int b2_stream_query(b2_stream_t s);
 int b2_event_create(b2_event_t* e);
 int b2_event_destroy(b2_event_t e);
 int b2_event_record(b2_event_t e, b2_stream_t s);
@@ -246,6 +249,15 @@ size_t b2_lm_head_noalloc_max_keys(void);
 int b2_lm_head_argmax_noalloc(const float* x, int ldx, int M, int K, int V, const void* table,
                               const float* scales, int wtype, const float* norm_w, float eps,
                               float* logits, int ldl, int* tokens, b2_stream_t s);
+
+/* Vocab-sharded lm_head: keys [M][parts] from b2_gemm(B2_EPI_ARGMAX) over a
+ * vocab slice starting at index_offset -> out[M], each row's largest key with
+ * its index rewritten as a global vocab index (an all-reduce MAX of these
+ * over the ranks gives the global argmax, lowest index on ties). */
+int b2_argmax_keys_merge(const unsigned long long* keys, int M, int parts, unsigned index_offset,
+                         unsigned long long* out, b2_stream_t s);
+/* tokens[i] = vocab index of keys[i], i < n. */
+int b2_keys_tokens(const unsigned long long* keys, int n, int* tokens, b2_stream_t s);
 
 /* Device-side greedy loop bookkeeping, run once per step after the argmax:
  * hist[loop[2]] = loop[0] (the token just produced, which is also the next

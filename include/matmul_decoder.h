@@ -368,6 +368,23 @@ int matmul_decoder_batch_step(MatmulDecoderBatch* b, const int* tokens_in, int* 
 void matmul_decoder_batch_get_stats(const MatmulDecoderBatch* b, MatmulDecoderStats* stats);
 void matmul_decoder_batch_destroy(MatmulDecoderBatch* b);
 
+/* ─── ADDITIVE: vocab-sharded lm_head over ranks (one GPU each) ───
+ * The sequences of a batch are split over ranks; each rank runs its own
+ * MatmulDecoderBatch on its GPU.  After sharding, each rank keeps the lm_head
+ * rows of one slice of the vocabulary: a step gathers every rank's final
+ * hidden rows (NCCL all-gather over NVLink), scores all rows against the
+ * local slice, and an NCCL all-reduce MAX of packed (value, index) keys gives
+ * every row its global argmax (lowest index on ties).  Every rank must call
+ * matmul_decoder_batch_step the same number of times.  logits_out is not
+ * available on a sharded decoder (MATMUL_DECODER_ERR_UNSUPPORTED). */
+
+/* 128-byte NCCL unique id: made once (rank 0) and passed to every rank. */
+int matmul_decoder_nccl_unique_id(void* id_out);
+/* Collective over the `world` ranks (each calls it with its rank).
+ * rows_per_rank >= the decoder's n_seqs and equal on every rank. */
+int matmul_decoder_batch_shard_vocab(MatmulDecoderBatch* b, int rank, int world, const void* nccl_id,
+                                     int rows_per_rank);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,9 +20,9 @@
 //
 // The eight consumer warps take the operations in order.  A data operation's
 // tiles are split over the warps by K range (each warp a slice of every
-// tile's 64-byte super-blocks, on the tensor cores: mma.m16n8k16 with the
-// weight rows as the A operand and the staged FP16 activation as the B
-// operand); the partial sums meet in shared memory after one barrier.  Every
+// tile's 64-byte super-blocks; FP16 x FP16 products accumulated in FP32 with
+// the mixed-precision FMA); the partial sums meet in shared memory after one
+// barrier.  Every
 // barrier on this path is a vote, so a failed wait anywhere turns into a
 // failed vote and the whole CTA stops together.
 //
@@ -229,29 +229,23 @@ __device__ __forceinline__ ulonglong2 ll_get2(const unsigned long long* p) {
 __device__ __forceinline__ bool ll_ok(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 __device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
-// ─── tensor-core row dots over a tile-major 16-row tile ───
+// ─── row dots over a tile-major 16-row tile (CUDA cores) ───
 //
 // A tile is [super-block][16 rows][64 bytes].  Lane (g = lane / 4, q = lane
 // % 4) reads the 16 bytes at offset 16 q of rows g and g + 8 of every
 // super-block; the eight lanes of one shared-memory wavefront read 128
-// consecutive bytes, so the loads are conflict-free.  Inside a super-block
-// the k order is permuted identically for the weights and the staged
-// activation (which a dot product does not see); INT8 / INT4 widen to FP16
-// exactly with byte permutes (value + 1024 in the mantissa of 1024, one
-// half2 subtraction removes the bias).
+// consecutive bytes, so the loads are conflict-free.  The products are FP16
+// weight x FP16 activation, exact in FP32, added into FP32 accumulators by
+// the mixed-precision fma.rn.f32.f16 (one rounding per addition, the FP32
+// accumulation the reference's matmul semantics ask for).  INT8 / INT4 widen
+// to FP16 exactly with byte permutes (value + 1024 in the mantissa of 1024,
+// one half2 subtraction removes the bias).  Legacy mma.sync would waste 7 of
+// its 8 columns on a single activation vector and runs at a fraction of the
+// FMA pipes' rate on this part.
 
 template <int WT>
 __host__ __device__ constexpr int sb_k() {
     return WT == B2_W_F16 ? 32 : WT == B2_W_I8 ? 64 : 128;
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
@@ -259,80 +253,72 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t*>(&r);
 }
 
+// a0 += w.lo * x.lo, a1 += w.hi * x.hi (FP16 operands, FP32 accumulators)
+__device__ __forceinline__ void fma2h(float& a0, float& a1, uint32_t w, uint32_t x) {
+    asm("{\n .reg .b16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %2;\n mov.b32 {xl, xh}, %3;\n"
+        " fma.rn.f32.f16 %0, wl, xl, %0;\n fma.rn.f32.f16 %1, wh, xh, %1;\n}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(w), "r"(x));
+}
+
+// One 16-byte chunk of weights (w) against its activations (x: 16 bytes for
+// FP16, 32 for INT8, 64 for INT4, as half2 words in the matching k order).
 template <int WT>
-__device__ __forceinline__ void sb_mma(float (&d0)[4], float (&d1)[4], const uint4 wg, const uint4 wh,
-                                       const uint32_t* xw) {
-    const uint32_t* g = &wg.x;
-    const uint32_t* h = &wh.x;
+__device__ __forceinline__ void chunk_fma(float& a0, float& a1, const uint4 w, const uint32_t* x) {
+    const uint32_t* u = &w.x;
     if constexpr (WT == B2_W_F16) {
-        mma16816(d0, g[0], h[0], g[1], h[1], xw[0], xw[1]);
-        mma16816(d1, g[2], h[2], g[3], h[3], xw[2], xw[3]);
+#pragma unroll
+        for (int t = 0; t < 4; t++) fma2h(a0, a1, u[t], x[t]);
     } else if constexpr (WT == B2_W_I8) {
         const uint32_t bias = 0x64806480u;  // half2(1152, 1152) = 1024 + 128
 #pragma unroll
         for (int t = 0; t < 4; t++) {
-            const uint32_t ug = g[t] ^ 0x80808080u, uh = h[t] ^ 0x80808080u;
-            const uint32_t glo = hsub2_u32(__byte_perm(ug, 0x64646464u, 0x4140), bias);
-            const uint32_t ghi = hsub2_u32(__byte_perm(ug, 0x64646464u, 0x4342), bias);
-            const uint32_t hlo = hsub2_u32(__byte_perm(uh, 0x64646464u, 0x4140), bias);
-            const uint32_t hhi = hsub2_u32(__byte_perm(uh, 0x64646464u, 0x4342), bias);
-            mma16816(t & 1 ? d1 : d0, glo, hlo, ghi, hhi, xw[2 * t], xw[2 * t + 1]);
+            const uint32_t b = u[t] ^ 0x80808080u;
+            fma2h(a0, a1, hsub2_u32(__byte_perm(b, 0x64646464u, 0x4140), bias), x[2 * t]);
+            fma2h(a0, a1, hsub2_u32(__byte_perm(b, 0x64646464u, 0x4342), bias), x[2 * t + 1]);
         }
     } else {
         const uint32_t bias = 0x64086408u;  // half2(1032, 1032) = 1024 + 8
 #pragma unroll
         for (int t = 0; t < 4; t++) {
-            const uint32_t ug = g[t] ^ 0x88888888u, uh = h[t] ^ 0x88888888u;
-            // word t holds k = 8t + i at nibble i; half2 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7)
-            mma16816(d0, hsub2_u32((ug & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32((uh & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32(((ug >> 4) & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32(((uh >> 4) & 0x000F000Fu) | 0x64006400u, bias), xw[4 * t], xw[4 * t + 1]);
-            mma16816(d1, hsub2_u32(((ug >> 8) & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32(((uh >> 8) & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32(((ug >> 12) & 0x000F000Fu) | 0x64006400u, bias),
-                     hsub2_u32(((uh >> 12) & 0x000F000Fu) | 0x64006400u, bias), xw[4 * t + 2], xw[4 * t + 3]);
+            // word t holds k = 8t + i at nibble i; half2 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7),
+            // the order the INT4 activation staging uses
+            const uint32_t b = u[t] ^ 0x88888888u;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                fma2h(a0, a1, hsub2_u32(((b >> (4 * j)) & 0x000F000Fu) | 0x64006400u, bias), x[4 * t + j]);
         }
     }
 }
 
-// Rows g and g + 8 of a tile over super-blocks [sb0, sb1) against xs.
+// Rows g and g + 8 of a tile over super-blocks [sb0, sb1) against xs; the
+// sums over the four lanes of a row are reduced, every lane returns them.
 template <int WT>
-__device__ __noinline__ void tile_dot(const unsigned char* tile, const __half* xs, int sb0, int sb1, int lane,
+__device__ __forceinline__ void tile_dot(const unsigned char* tile, const __half* xs, int sb0, int sb1, int lane,
                                       float& y0, float& y1) {
-    constexpr int SK = sb_k<WT>(), XW = SK / 8;
+    constexpr int SK = sb_k<WT>(), XW = SK / 8;  // activation words (half2) per lane per super-block
     const int q = lane & 3;
     const unsigned char* pa = tile + (lane >> 2) * 64 + q * 16;
     const __half* px = xs + q * (SK / 4);
-    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-    float d2[4] = {0.f, 0.f, 0.f, 0.f}, d3[4] = {0.f, 0.f, 0.f, 0.f};
-    int sb = sb0;
-    for (; sb + 1 < sb1; sb += 2) {
-        const uint4 wg0 = *reinterpret_cast<const uint4*>(pa + sb * 1024);
-        const uint4 wh0 = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 512);
-        const uint4 wg1 = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 1024);
-        const uint4 wh1 = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 1536);
-        uint32_t x0[XW], x1[XW];
-#pragma unroll
-        for (int i = 0; i < XW / 4; i++) {
-            *reinterpret_cast<uint4*>(x0 + 4 * i) = *reinterpret_cast<const uint4*>(px + sb * SK + 8 * i);
-            *reinterpret_cast<uint4*>(x1 + 4 * i) = *reinterpret_cast<const uint4*>(px + (sb + 1) * SK + 8 * i);
-        }
-        sb_mma<WT>(d0, d1, wg0, wh0, x0);
-        sb_mma<WT>(d2, d3, wg1, wh1, x1);
-    }
-    if (sb < sb1) {
-        const uint4 wg0 = *reinterpret_cast<const uint4*>(pa + sb * 1024);
-        const uint4 wh0 = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 512);
-        uint32_t x0[XW];
+    float g0 = 0.f, g1 = 0.f, h0 = 0.f, h1 = 0.f;
+#pragma unroll 2
+    for (int sb = sb0; sb < sb1; sb++) {
+        const uint4 wg = *reinterpret_cast<const uint4*>(pa + sb * 1024);
+        const uint4 wh = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 512);
+        uint32_t xw[XW];
 #pragma unroll
         for (int i = 0; i < XW / 4; i++)
-            *reinterpret_cast<uint4*>(x0 + 4 * i) = *reinterpret_cast<const uint4*>(px + sb * SK + 8 * i);
-        sb_mma<WT>(d0, d1, wg0, wh0, x0);
+            *reinterpret_cast<uint4*>(xw + 4 * i) = *reinterpret_cast<const uint4*>(px + sb * SK + 8 * i);
+        chunk_fma<WT>(g0, g1, wg, xw);
+        chunk_fma<WT>(h0, h1, wh, xw);
     }
-    // all 8 columns hold the same sums: column 2q of rows g and g + 8
-    y0 = (d0[0] + d1[0]) + (d2[0] + d3[0]);
-    y1 = (d0[2] + d1[2]) + (d2[2] + d3[2]);
+    float a = g0 + g1, b = h0 + h1;
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    b += __shfl_xor_sync(0xffffffffu, b, 1);
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    b += __shfl_xor_sync(0xffffffffu, b, 2);
+    y0 = a;
+    y1 = b;
 }
 
 __host__ __device__ inline int row_bytes(int wtype, int K) {
@@ -354,7 +340,7 @@ __device__ __forceinline__ int stage_pos(int e) {
 // sh.mrg_m / mrg_l / mrg_o.  Scores of the 8 positions x 2 heads are reduced
 // across the warp in a transposed butterfly: afterwards lane l holds the
 // score with index (l >> 1) & 15 = 2 i + h.
-__device__ __noinline__ void attend8(Sh& sh, const unsigned char* kb, const unsigned char* vb, int n, int warp,
+__device__ __forceinline__ void attend8(Sh& sh, const unsigned char* kb, const unsigned char* vb, int n, int warp,
                                      int lane) {
     const float scale = 0.08838834764831845f;  // 1/sqrt(128)
     float qv[kGq][4], ao[kGq][4], am[kGq], al[kGq];

@@ -344,3 +344,53 @@ extern "C" int b2_lm_head_argmax_noalloc(const float* x, int ldx, int M, int K, 
     if (e != cudaSuccess) return b2_set_error(B2_ERR_CUDA, "b2_argmax_final: %s", cudaGetErrorString(e));
     return 0;
 }
+
+// ─── vocab-sharded lm_head: keys across ranks ───
+//
+// With the vocabulary split over ranks, each rank's lm_head GEMM leaves per
+// CTA keys (orderable value << 32 | ~local index) for every row.  The merge
+// keeps each row's largest key and rewrites its index as a global vocab index
+// (local + offset), so an all-reduce MAX over the ranks picks the largest
+// logit and, among equal logits, the lowest global index: the first maximum
+// of the reference argmax (src/cpu_ops.c:575-586).
+namespace {
+
+__global__ void __launch_bounds__(128) keys_merge_kernel(const unsigned long long* __restrict__ keys, int parts,
+                                                         unsigned offset, unsigned long long* __restrict__ out) {
+    unsigned long long k = 0ull;
+    for (int i = threadIdx.x; i < parts; i += blockDim.x) {
+        const unsigned long long v = keys[(size_t)blockIdx.x * parts + i];
+        k = v > k ? v : k;
+    }
+    k = b2::warp_max_u64(k);
+    __shared__ unsigned long long w[4];
+    if ((threadIdx.x & 31) == 0) w[threadIdx.x >> 5] = k;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < 4; i++) k = w[i] > k ? w[i] : k;
+        k = w[0] > k ? w[0] : k;
+        const uint32_t idx = b2::key_index(k) + offset;
+        out[blockIdx.x] = (k & 0xFFFFFFFF00000000ull) | (0xFFFFFFFFull - idx);
+    }
+}
+
+__global__ void keys_tokens_kernel(const unsigned long long* __restrict__ keys, int n, int* __restrict__ tokens) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) tokens[i] = (int)b2::key_index(keys[i]);
+}
+
+}  // namespace
+
+extern "C" int b2_argmax_keys_merge(const unsigned long long* keys, int M, int parts, unsigned index_offset,
+                                    unsigned long long* out, b2_stream_t s) {
+    if (!keys || !out || M <= 0 || parts <= 0)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_argmax_keys_merge: bad arguments");
+    keys_merge_kernel<<<M, 128, 0, (cudaStream_t)s>>>(keys, parts, index_offset, out);
+    return b2_check_launch("b2_argmax_keys_merge");
+}
+
+extern "C" int b2_keys_tokens(const unsigned long long* keys, int n, int* tokens, b2_stream_t s) {
+    if (!keys || !tokens || n <= 0) return b2_set_error(B2_ERR_INVALID_ARG, "b2_keys_tokens: bad arguments");
+    keys_tokens_kernel<<<(n + 127) / 128, 128, 0, (cudaStream_t)s>>>(keys, n, tokens);
+    return b2_check_launch("b2_keys_tokens");
+}

@@ -121,6 +121,13 @@ int b2_stream_sync(b2_stream_t s) {
     return 0;
 }
 
+int b2_stream_query(b2_stream_t s) {
+    const cudaError_t e = cudaStreamQuery((cudaStream_t)s);
+    if (e == cudaSuccess) return 0;
+    if (e == cudaErrorNotReady) return 1;
+    return b2_set_error(B2_ERR_CUDA, "cudaStreamQuery: %s", cudaGetErrorString(e));
+}
+
 int b2_event_create(b2_event_t* e) {
     cudaEvent_t ev;
     B2_TRY(cudaEventCreate(&ev));

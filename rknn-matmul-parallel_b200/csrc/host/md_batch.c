@@ -10,10 +10,13 @@
  * own position, and the lm_head + argmax produce one token per sequence.
  * Token ids and positions travel in a small pinned block per step.
  */
+#include <dlfcn.h>
+#include <nccl.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #include <time.h>
+#include <unistd.h>
 
 #include "md_internal.h"
 
@@ -37,7 +40,58 @@ struct MatmulDecoderBatch {
     b2_graph_t graph;
     b2_event_t ev[3];
     MatmulDecoderStats stats;
+    /* vocab-sharded lm_head (matmul_decoder_batch_shard_vocab) */
+    int world, rank, rows;          /* ranks, this rank, rows each rank contributes (>= n) */
+    int v0, v1;                     /* this rank's vocabulary slice */
+    ncclComm_t comm;
+    void* shard_buf;                /* one allocation for the buffers below */
+    uint16_t* g_x16;                /* [world * rows][H] final-normed FP16 rows of every rank */
+    unsigned long long* g_keys;     /* lm_head GEMM keys [world * rows][parts] */
+    unsigned long long* m_keys;     /* merged keys [world * rows] (global indices) */
+    int* g_tok;                     /* tokens of the local GEMM (unused) */
 };
+
+/* ─── NCCL, loaded at run time ───
+ * libnccl.so.2 is opened when the first sharded decoder is set up; in a
+ * process that already uses NCCL (torch.distributed) this is that library. */
+static struct {
+    void* h;
+    ncclResult_t (*get_id)(ncclUniqueId*);
+    ncclResult_t (*init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*destroy)(ncclComm_t);
+    ncclResult_t (*abort_)(ncclComm_t);
+    ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*);
+    const char* (*error_string)(ncclResult_t);
+} g_nccl;
+
+static int nccl_load(void) {
+    if (g_nccl.h) return 0;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        MD_LOG("NCCL not found: %s\n", dlerror());
+        return MATMUL_DECODER_ERR_UNSUPPORTED;
+    }
+#define NCCL_SYM(field, name)                                    \
+    *(void**)&g_nccl.field = dlsym(h, name);                     \
+    if (!g_nccl.field) {                                         \
+        MD_LOG("NCCL symbol %s missing\n", name);                \
+        return MATMUL_DECODER_ERR_UNSUPPORTED;                   \
+    }
+    NCCL_SYM(get_id, "ncclGetUniqueId");
+    NCCL_SYM(init_rank, "ncclCommInitRank");
+    NCCL_SYM(all_gather, "ncclAllGather");
+    NCCL_SYM(all_reduce, "ncclAllReduce");
+    NCCL_SYM(destroy, "ncclCommDestroy");
+    NCCL_SYM(abort_, "ncclCommAbort");
+    NCCL_SYM(async_error, "ncclCommGetAsyncError");
+    NCCL_SYM(error_string, "ncclGetErrorString");
+#undef NCCL_SYM
+    g_nccl.h = h;
+    return 0;
+}
 
 static double now_ms(void) {
     struct timespec ts;
@@ -66,6 +120,8 @@ void matmul_decoder_batch_destroy(MatmulDecoderBatch* b) {
     b2_stream_destroy(b->stream);
     b2_host_free(b->h_blk);
     b2_host_free(b->h_tok);
+    if (b->comm) g_nccl.destroy(b->comm);
+    if (b->shard_buf) b2_free(b->shard_buf);
     free(b->seq_len);
     md_model_free(&b->model);
     free(b);
@@ -224,6 +280,12 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
                        b->attn_block, b->d_tok + n};
     if (!rc) rc = md_enqueue_layers(m, &lb, n, &kv, s);
     if (!rc) rc = b2_event_record(b->ev[1], s);
+    if (!rc && b->comm) {
+        /* sharded lm_head: this rank's final-normed rows into its slot of the
+         * gathered buffer; the collectives run outside the graph */
+        return b2_rows_to_f16(b->g_x16 + (size_t)b->rank * b->rows * H, H, b->hidden, H, n, H, m->final_norm,
+                              c->rms_eps, s);
+    }
     if (!rc && b->x16 && n >= 16 && (m->lm_wtype == B2_W_I8 || m->lm_wtype == B2_W_F16) && H % 64 == 0) {
         /* many sequences: the lm_head is a GEMM on the tensor cores with the argmax in its epilogue */
         rc = b2_rows_to_f16(b->x16, H, b->hidden, H, n, H, m->final_norm, c->rms_eps, s);
@@ -237,6 +299,120 @@ static int batch_enqueue(MatmulDecoderBatch* b) {
     if (!rc) rc = b2_memcpy_d2h(b->h_tok, b->d_tok, (size_t)(n + 1) * 4, s);
     if (!rc) rc = b2_event_record(b->ev[2], s);
     return rc;
+}
+
+/* Sharded lm_head tail of a step (enqueued after the graph):
+ *   all-gather of every rank's final-normed FP16 rows,
+ *   the INT8 (or FP16) lm_head GEMM over this rank's vocab slice for all rows,
+ *   per-row merge of the GEMM's keys with global vocab indices,
+ *   all-reduce MAX of the keys over the ranks, and this rank's tokens.
+ * Then a bounded wait: the stream is polled together with the communicator's
+ * asynchronous error state, and a wait longer than B2_NCCL_TIMEOUT_S seconds
+ * (default 120) aborts the communicator instead of hanging. */
+static int shard_head(MatmulDecoderBatch* b) {
+    DevModel* m = &b->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    const int H = c->hidden_dim, M = b->world * b->rows, Nv = b->v1 - b->v0;
+    cudaStream_t cs = (cudaStream_t)b->stream;
+    ncclResult_t nr = g_nccl.all_gather(b->g_x16 + (size_t)b->rank * b->rows * H, b->g_x16, (size_t)b->rows * H * 2,
+                                        ncclUint8, b->comm, cs);
+    if (nr != ncclSuccess) {
+        MD_LOG("ncclAllGather: %s\n", g_nccl.error_string(nr));
+        return MATMUL_DECODER_ERR_RKNN;
+    }
+    const size_t wrow = m->lm_wtype == B2_W_I8 ? (size_t)H : (size_t)H * 2;
+    B2GemmArgs g = {NULL, 0, b->g_x16, H, M, H, Nv, (const unsigned char*)m->lm + (size_t)b->v0 * wrow,
+                    m->lm_wtype == B2_W_I8 ? m->lm_scales + b->v0 : NULL, m->lm_wtype, B2_EPI_ARGMAX, b->g_keys,
+                    b->g_tok, NULL, 0};
+    int rc = b2_gemm(&g, b->stream);
+    if (!rc) rc = b2_argmax_keys_merge(b->g_keys, M, (Nv + 127) / 128, (unsigned)b->v0, b->m_keys, b->stream);
+    if (rc) return rc;
+    nr = g_nccl.all_reduce(b->m_keys, b->m_keys, (size_t)M, ncclUint64, ncclMax, b->comm, cs);
+    if (nr != ncclSuccess) {
+        MD_LOG("ncclAllReduce: %s\n", g_nccl.error_string(nr));
+        return MATMUL_DECODER_ERR_RKNN;
+    }
+    rc = b2_keys_tokens(b->m_keys + (size_t)b->rank * b->rows, b->n, b->d_tok, b->stream);
+    if (!rc) rc = b2_memcpy_d2h(b->h_tok, b->d_tok, (size_t)(b->n + 1) * 4, b->stream);
+    if (!rc) rc = b2_event_record(b->ev[2], b->stream);
+    if (rc) return rc;
+    const char* to = getenv("B2_NCCL_TIMEOUT_S");
+    const double limit_ms = (to && atof(to) > 0 ? atof(to) : 120.0) * 1e3, t0 = now_ms();
+    for (;;) {
+        const int q = b2_stream_query(b->stream);
+        if (q == 0) return 0;
+        if (q < 0) return q;
+        ncclResult_t ae = ncclSuccess;
+        g_nccl.async_error(b->comm, &ae);
+        if ((ae != ncclSuccess && ae != ncclInProgress) || now_ms() - t0 > limit_ms) {
+            MD_LOG("sharded lm_head: %s; aborting the communicator\n",
+                   ae != ncclSuccess ? g_nccl.error_string(ae) : "timed out");
+            g_nccl.abort_(b->comm);
+            b->comm = NULL;
+            return MATMUL_DECODER_ERR_RKNN;
+        }
+        usleep(20);
+    }
+}
+
+int matmul_decoder_nccl_unique_id(void* id_out) {
+    if (!id_out) return MATMUL_DECODER_ERR_INVALID_ARG;
+    int rc = nccl_load();
+    if (rc) return rc;
+    ncclUniqueId id;
+    const ncclResult_t nr = g_nccl.get_id(&id);
+    if (nr != ncclSuccess) {
+        MD_LOG("ncclGetUniqueId: %s\n", g_nccl.error_string(nr));
+        return MATMUL_DECODER_ERR_RKNN;
+    }
+    memcpy(id_out, &id, sizeof(id));
+    return MATMUL_DECODER_OK;
+}
+
+int matmul_decoder_batch_shard_vocab(MatmulDecoderBatch* b, int rank, int world, const void* nccl_id,
+                                     int rows_per_rank) {
+    if (!b || !nccl_id || world < 1 || rank < 0 || rank >= world || rows_per_rank < b->n || b->comm)
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    DevModel* m = &b->model;
+    const MatmulDecoderConfig* c = &m->cfg;
+    const int H = c->hidden_dim, V = c->vocab_size;
+    if ((m->lm_wtype != B2_W_I8 && m->lm_wtype != B2_W_F16) || H % 64 || (long long)world * rows_per_rank > 4096)
+        return MATMUL_DECODER_ERR_UNSUPPORTED;
+    int rc = nccl_load();
+    if (rc) return rc;
+    b2_set_device(b->device);
+    b->world = world;
+    b->rank = rank;
+    b->rows = rows_per_rank;
+    b->v0 = (int)((long long)V * rank / world);
+    b->v1 = (int)((long long)V * (rank + 1) / world);
+    const size_t M = (size_t)world * rows_per_rank, parts = (size_t)(b->v1 - b->v0 + 127) / 128;
+    const size_t bx = (M * H * 2 + 255) & ~(size_t)255, bk = (M * parts * 8 + 255) & ~(size_t)255;
+    const size_t bm = (M * 8 + 255) & ~(size_t)255;
+    rc = b2_malloc(&b->shard_buf, bx + bk + bm + M * 4 + 256);
+    if (rc) return MATMUL_DECODER_ERR_MEMORY;
+    unsigned char* p = (unsigned char*)b->shard_buf;
+    b->g_x16 = (uint16_t*)p;
+    b->g_keys = (unsigned long long*)(p + bx);
+    b->m_keys = (unsigned long long*)(p + bx + bk);
+    b->g_tok = (int*)(p + bx + bk + bm);
+    rc = b2_memset(b->g_x16, 0, bx, NULL);  /* pad rows stay zero */
+    if (!rc) rc = b2_stream_sync(NULL);
+    if (rc) return rc;
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    const ncclResult_t nr = g_nccl.init_rank(&b->comm, world, id, rank);
+    if (nr != ncclSuccess) {
+        MD_LOG("ncclCommInitRank: %s\n", g_nccl.error_string(nr));
+        b->comm = NULL;
+        return MATMUL_DECODER_ERR_RKNN;
+    }
+    /* the step graph changes: recapture without the replicated lm_head */
+    b2_graph_destroy(b->graph);
+    b->graph = NULL;
+    printf("[MatmulDecoder] Batch lm_head sharded: rank %d of %d, vocab [%d, %d), %d rows per rank\n", rank, world,
+           b->v0, b->v1, rows_per_rank);
+    return MATMUL_DECODER_OK;
 }
 
 int matmul_decoder_batch_step(MatmulDecoderBatch* b, const int* tokens_in, int* tokens_out, float* logits_out) {
@@ -269,7 +445,9 @@ int matmul_decoder_batch_step(MatmulDecoderBatch* b, const int* tokens_in, int* 
         b->h_blk[i] = tokens_in[i];
         b->h_blk[b->n + i] = b->seq_len[i];
     }
+    if (logits_out && b->comm) return MATMUL_DECODER_ERR_UNSUPPORTED;  /* a rank holds one vocab slice */
     rc = b2_graph_launch(b->graph, b->stream);
+    if (!rc && b->comm) rc = shard_head(b);
     if (!rc) rc = b2_stream_sync(b->stream);
     if (rc) {
         MD_LOG("batch step failed: %s\n", b2_last_error());

@@ -111,6 +111,8 @@ SIGNATURES = {
     "matmul_decoder_batch_step": (c_int, [c_vp, c_vp, c_vp, c_vp]),
     "matmul_decoder_batch_get_stats": (None, [c_vp, c_vp]),
     "matmul_decoder_batch_destroy": (None, [c_vp]),
+    "matmul_decoder_nccl_unique_id": (c_int, [c_vp]),
+    "matmul_decoder_batch_shard_vocab": (c_int, [c_vp, c_int, c_int, c_vp, c_int]),
     # b2_kernels.h
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_device_count": (c_int, [c_vp]),
@@ -129,6 +131,7 @@ SIGNATURES = {
     "b2_stream_create": (c_int, [c_vp]),
     "b2_stream_destroy": (c_int, [c_vp]),
     "b2_stream_sync": (c_int, [c_vp]),
+    "b2_stream_query": (c_int, [c_vp]),
     "b2_event_create": (c_int, [c_vp]),
     "b2_event_destroy": (c_int, [c_vp]),
     "b2_event_record": (c_int, [c_vp, c_vp]),
@@ -167,6 +170,8 @@ SIGNATURES = {
     "b2_mk2_decode": (c_int, [c_vp, c_vp]),
     "b2_mk2_final_hidden": (c_vp, [c_vp]),
     "b2_tile_relayout": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
+    "b2_argmax_keys_merge": (c_int, [c_vp, c_int, c_int, ctypes.c_uint, c_vp, c_vp]),
+    "b2_keys_tokens": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "b2_lm_head_argmax": (c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_int, c_vp, c_float,
                                   c_vp, c_int, c_vp, c_vp, c_vp]),
 }
@@ -187,6 +192,15 @@ def capi(path: str = LIB_PATH):
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL unique id (matmul_decoder_nccl_unique_id)."""
+    buf = ctypes.create_string_buffer(128)
+    rc = capi().matmul_decoder_nccl_unique_id(buf)
+    if rc != 0:
+        raise RuntimeError(f"matmul_decoder_nccl_unique_id failed ({rc})")
+    return buf.raw
 
 
 def check(rc: int, what: str = "call"):
@@ -374,6 +388,11 @@ class BatchDecoder:
         check(capi().matmul_decoder_batch_step(self.b, t.ctypes.data, out.ctypes.data, _ptr(logits)),
               "batch_step")
         return (out, logits) if want_logits else out
+
+    def shard_vocab(self, rank: int, world: int, nccl_id: bytes, rows_per_rank: int):
+        """matmul_decoder_batch_shard_vocab (collective over the ranks)."""
+        buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        check(capi().matmul_decoder_batch_shard_vocab(self.b, rank, world, buf, rows_per_rank), "batch_shard_vocab")
 
     def stats(self):
         s = MatmulDecoderStats()
