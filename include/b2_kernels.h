@@ -240,7 +240,11 @@ int b2_lm_head_argmax(const float* x, int ldx, int M, int K, int V, const void* 
  * above that (rows per CTA: 32 int8, 16 F16, 8 F32) are rejected with
  * ERR_INVALID_ARG.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress); make that first call before any stream
- * capture.  All calls on one device share its array and it keeps the last
+ * capture.  The looked-up address is cached per device ordinal for the life
+ * of the process and belongs to the device's primary context: after
+ * cudaDeviceReset (or any other teardown of that context) the cached address
+ * is stale, so the entry point must not be called again in that process.
+ * All calls on one device share its array and it keeps the last
  * call's contents: calls that may overlap on the GPU (e.g. on two streams of
  * the same device) race and must be serialized by the caller.  Every key a
  * call reads is written by the same call, so nothing needs clearing between
@@ -258,6 +262,21 @@ int b2_argmax_keys_merge(const unsigned long long* keys, int M, int parts, unsig
                          unsigned long long* out, b2_stream_t s);
 /* tokens[i] = vocab index of keys[i], i < n. */
 int b2_keys_tokens(const unsigned long long* keys, int n, int* tokens, b2_stream_t s);
+
+/* Token drawn from device logits[V] (FP32) after the lm_head, with the
+ * semantics of matmul_sample_token (csrc/host/md_generate.c; the reference's
+ * samplers are src/matmul_decoder.c:2316-2323 and src/cpu_ops.c:593-672):
+ * repeat_tokens (device, n_repeat entries) penalized once per occurrence,
+ * top_k == 1 greedy (first maximum, no temperature), else temperature, the
+ * top_k largest (all when top_k <= 0), the top_p prefix of those (top_p in
+ * (0, 1)), and a draw with weights exp(v - v_max) from the counter-based
+ * generator SplitMix64(seed, counter).  token (device int) gets the draw;
+ * info (device int[4], optional) gets [kept entries, K, threshold key, ties
+ * kept at the threshold].  One 8-CTA cluster; V <= b2_sample_max_vocab(). */
+size_t b2_sample_max_vocab(void);
+int b2_sample_token(const float* logits, int V, const int* repeat_tokens, int n_repeat, float repeat_penalty,
+                    int top_k, float top_p, float temperature, unsigned long long seed, unsigned long long counter,
+                    int* token, int* info, b2_stream_t s);
 
 /* Device-side greedy loop bookkeeping, run once per step after the argmax:
  * hist[loop[2]] = loop[0] (the token just produced, which is also the next

@@ -299,6 +299,20 @@ int matmul_decoder_export_hf_model(const char* hf_model_path,
 int matmul_decoder_step_token(MatmulDecoderContext* ctx, int token_id,
                               const float* embedding);
 
+/* ADDITIVE.  One decode step, then the token drawn on the device from its
+ * logits (b2_sample_token) with the semantics of matmul_sample_token:
+ * repeat penalty per listed occurrence, top_k == 1 greedy, temperature,
+ * top-k, top-p, then a draw with probability proportional to
+ * exp(v - v_max).  Only the token crosses to the host.  Draw i of a context
+ * is a function of (seed, i): the seed comes from rand() at creation (so
+ * srand() before create fixes it) or from matmul_decoder_set_seed, which also
+ * restarts i at 0.  top_k == 1 without a penalty is the greedy step
+ * (matmul_decoder_step_token).  matmul_decoder_generate draws every token
+ * this way.  Returns the token or a negative error. */
+int matmul_decoder_step_sample(MatmulDecoderContext* ctx, int token_id, const float* embedding,
+                               const SamplingParams* params);
+int matmul_decoder_set_seed(MatmulDecoderContext* ctx, unsigned long long seed);
+
 /* ADDITIVE.  Greedy decode of n_tokens tokens with the token feedback kept on
  * the device: step i consumes the token produced by step i-1 (step 0 consumes
  * first_token), so the host neither copies a token nor synchronizes between

@@ -1510,15 +1510,18 @@ static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB per-
 template <int WT>
 int launch(const B2MkPlan* p, cudaStream_t s) {
     auto fn = mk_decode_kernel<WT>;
-    static thread_local int configured[8] = {0};
+    constexpr int kMaxDevices = 64;
+    static thread_local int configured[kMaxDevices] = {0};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (!configured[dev & 7]) {
+    B2_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_mk_decode: device ordinal %d above %d", dev, kMaxDevices - 1);
+    if (!configured[dev]) {
         B2_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
         int per_sm = 0;
         B2_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, kSmemBytes));
         if (per_sm < 1) return b2_set_error(B2_ERR_CUDA, "b2_mk_decode: kernel does not fit on an SM");
-        configured[dev & 7] = 1;
+        configured[dev] = 1;
     }
     int sms = 0;
     B2_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -27,32 +27,34 @@
 // failed vote and the whole CTA stops together.
 //
 // Per layer l (the phases other CTAs depend on):
-//   XIN(l)   wait for the DN(l-1) flag of every CTA; x = sum of the
-//            layer-output copies; RMSNorm -> FP16 rows input
-//   QKV      tiles of q|k|v rows; results published as LL words (an FP32
-//            value and the step tag in one 64-bit store, which readers poll)
+//   XIN(l)   poll the layer-(l-1) output words (LL words: an FP32 value and
+//            a tag of step and layer in one 64-bit store, which readers poll); RMSNorm
+//            -> FP16 rows input
+//   QKV      tiles of q|k|v rows; results published as LL words
 //   unit (kv head g, o_proj row slice r), on nkv * (G / nkv) CTAs:
 //     AIN    poll the q|k|v words of head group g; q/k RMSNorm, RoPE; unit r = 0
 //            appends the new K/V row to the cache
 //     KV     cached positions of head g, online softmax per warp
 //     AOUT   the newest position, merge of the warps, FP16 attention output
 //     O      o_proj tiles of rows in slice r, columns of group g: partial sums
-//            (plus the residual, in the g = 0 units) added into h_mid
-//     OEND   set this unit's AO(l) flag
-//   GIN(l)   wait for the AO(l) flag of every unit; RMSNorm(h_mid) -> FP16
+//            published as LL words (one partial per kv head and output)
+//   RO       reducer: for the ~hidden/G outputs this CTA owns, the nkv
+//            partials in head order plus the residual x -> h_mid words
+//   GIN(l)   poll every h_mid word; RMSNorm(h_mid) -> FP16
 //   GU       tiles of 8 channels (gate and up rows interleaved): SiLU(g) * u
 //   DN       the same channels' rows of the input-major down weight times
 //            SiLU(g) * u: a partial of every output
-//   DEND     partial (and, on CTA 0, the residual h_mid) added into one of
-//            four copies of the layer output; set this CTA's DN(l) flag
+//   DEND     the CTA's down partial of every output as LL words
+//   RD       reducer: for the outputs this CTA owns, every CTA's partial in
+//            CTA order plus the residual h_mid -> layer-output words
 // then LIN / LM / LEND (final norm, lm_head tiles, argmax keys) and the
 // last CTA to finish publishes the token.
 //
-// Flags hold the tag (generation + 1) of the step that set them, where the
-// generation (state[B2_MK_GEN]) counts completed launches; one word per CTA
-// (or unit) avoids the serialization of many atomic additions on one
-// counter.  Every wait is bounded (plan->poll_limit polls): on timeout the CTA
-// sets state[B2_MK_ERR], stops, lets its in-flight copies land and returns.
+// Sums run in a fixed order, so a step's result does not depend on timing.
+// Tags are the generation + 1 of the step that wrote the word, where the
+// generation (state[B2_MK_GEN]) counts completed launches.  Every wait is
+// bounded (plan->poll_limit polls): on timeout the CTA sets state[B2_MK_ERR],
+// stops, lets its in-flight copies land and returns.
 #include "b2_common.cuh"
 
 namespace {
@@ -69,14 +71,15 @@ constexpr int kKVPos = 64;             // cached positions per K/V operation
 constexpr int kMaxH = 4 * kCons;       // hidden: one float4 per consumer thread
 constexpr int kMaxF = 3072;            // longest staged activation
 constexpr int kMaxCh = 32;             // gate|up channels per CTA
-constexpr int kOutCopies = 4;          // copies of each layer-output accumulator
+constexpr int kOwn = 8;                // outputs each reducer CTA owns (CTAs 0 .. hidden / 8 - 1)
 constexpr int kFuseMax = 512;          // cached positions the host routes here
-constexpr int kMaxG = 256;             // CTAs the flag arrays have room for
+constexpr int kMaxG = 256;             // CTAs the partial arrays have room for
+constexpr int kMaxLayers = 32;         // layers of the shared-memory pointer table
 constexpr long long kDefaultPolls = 1ll << 22;
 static_assert(kCons == kGq * kHD, "the attention merge gives one consumer thread per (q head, dim)");
 
 enum Op : int {
-    OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_O, OP_OEND, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND,
+    OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_O, OP_RO, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND, OP_RD,
     OP_LIN, OP_LM, OP_LEND, OP_PFIN, OP_DONE
 };
 
@@ -104,30 +107,40 @@ struct Sh {
     float mrg_m[NC][kGq], mrg_l[NC][kGq];  // per-warp softmax state: max, sum
     float mrg_o[NC][kGq][kHD];             // ... and output
     float act[kMaxCh];          // FP16-rounded SiLU(gate) * up of this CTA's channels
-    float xres[kMaxH];          // layer input x (the o_proj residual)
+    float xres[kMaxH];          // x (layer input: the h_mid residual), then h_mid (the x residual)
     __half xs[2][kMaxF];        // staged FP16 inputs: [0] q|k|v and lm_head, [1] gate|up
     __half xo[kGq * kHD];       // attention output of the unit (o_proj input)
+    B2MkLayer lay[kMaxLayers];  // the per-layer pointer table (read by every operation)
 };
 
-constexpr int kRing = 192 * 1024;
+constexpr int kRing = 184 * 1024;
 constexpr size_t kSmemBytes = (size_t)kRing + sizeof(Sh) + 128;
 static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB per-block limit");
 
 // ─── scratch in global memory ───
 
+// Every vector passed between CTAs is a set of LL words (a value and a tag
+// in one 64-bit store); partial sums are reduced by the CTA that owns the
+// output (outputs split evenly over the CTAs), in a fixed order.  All layers
+// share one slot per vector, told apart by the tag (step generation and
+// layer), so the words stay resident in L2 across layers.  A slot is reused
+// only after every reader of the previous layer's words has moved on: each
+// phase that writes a slot for layer l + 1 runs after XIN(l + 1), which
+// needs every CTA's RD(l), which in every CTA follows its reads of layer l.
 struct Scr {
-    unsigned long long* cnt;  // [8]: [0] CTAs finished, [1] best key
-    unsigned* fdn;            // [L][kMaxG] DN(l) done: the step's tag, one word per CTA
-    unsigned* fao;            // [L][kMaxG] AO(l) done: the step's tag, one word per unit
-    float* hacc;              // [L][2][kOutCopies][H] layer outputs (two step parities)
-    float* macc;              // [L][2][H] h_mid (attention output + residual)
-    unsigned long long* qkv;  // LL [L][nqkv]
-    float* hfinal;            // [H]
+    unsigned long long* cnt;   // [8]: [0] CTAs finished, [1] best key
+    unsigned long long* qkv;   // LL [nqkv]
+    unsigned long long* opart; // LL [nkv][H] o_proj partials, one per kv head
+    unsigned long long* hmid;  // LL [H] h_mid = x + o_proj(attention)
+    unsigned long long* dpart; // LL [H / kOwn][kMaxG][kOwn] down partials by reducer, then source CTA
+    unsigned long long* dcnt;  // down partials published since the scratch was cleared
+    unsigned long long* xout;  // LL [H] layer output = h_mid + down(act)
+    float* hfinal;             // [H]
 };
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-__host__ __device__ inline Scr scr_layout(void* base, int L, int H, int nqkv, size_t* total) {
+__host__ __device__ inline Scr scr_layout(void* base, int L, int H, int nqkv, int nkv, size_t* total) {
     unsigned char* p = static_cast<unsigned char*>(base);
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -137,11 +150,13 @@ __host__ __device__ inline Scr scr_layout(void* base, int L, int H, int nqkv, si
     };
     Scr s;
     s.cnt = reinterpret_cast<unsigned long long*>(take(8 * 8));
-    s.fdn = reinterpret_cast<unsigned*>(take((size_t)L * kMaxG * 4));
-    s.fao = reinterpret_cast<unsigned*>(take((size_t)L * kMaxG * 4));
-    s.hacc = reinterpret_cast<float*>(take((size_t)L * 2 * kOutCopies * H * 4));
-    s.macc = reinterpret_cast<float*>(take((size_t)L * 2 * H * 4));
-    s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)L * nqkv * 8));
+    (void)L;
+    s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)nqkv * 8));
+    s.opart = reinterpret_cast<unsigned long long*>(take((size_t)nkv * H * 8));
+    s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)H * 8));
+    s.dpart = reinterpret_cast<unsigned long long*>(take((size_t)kMaxG * H * 8));
+    s.dcnt = reinterpret_cast<unsigned long long*>(take(8));
+    s.xout = reinterpret_cast<unsigned long long*>(take((size_t)H * 8));
     s.hfinal = reinterpret_cast<float*>(take((size_t)H * 4));
     if (total) *total = off;
     return s;
@@ -185,22 +200,6 @@ __device__ __forceinline__ unsigned long long atom_add_acqrel(unsigned long long
     asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
     return old;
 }
-__device__ __forceinline__ void st_release_u32(unsigned* p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint4 ld_acquire_v4(const unsigned* p) {
-    uint4 r;
-    asm volatile("ld.acquire.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p)
-                 : "memory");
-    return r;
-}
-__device__ __forceinline__ void red_add_v4(float* p, float4 v) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-                 : "memory");
-}
-__device__ __forceinline__ void red_add(float* p, float v) {
-    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
-}
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCons) : "memory"); }
 // Every barrier on the consumers' operation path is a vote (bar.red): a warp
 // that stops early takes part in the next barrier of the others with a false
@@ -220,6 +219,11 @@ __device__ __forceinline__ bool vote(bool pred) {
 __device__ __forceinline__ void ll_put(unsigned long long* p, float v, uint32_t tag) {
     const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_get(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 __device__ __forceinline__ ulonglong2 ll_get2(const unsigned long long* p) {
     ulonglong2 r;
@@ -291,34 +295,45 @@ __device__ __forceinline__ void chunk_fma(float& a0, float& a1, const uint4 w, c
     }
 }
 
-// Rows g and g + 8 of a tile over super-blocks [sb0, sb1) against xs; the
-// sums over the four lanes of a row are reduced, every lane returns them.
+// Rows g and g + 8 of T (<= 4) tiles, `stride` bytes apart, over
+// super-blocks [sb0, sb1) against xs.  The super-block loop is outermost, so
+// each activation chunk is loaded once for all tiles, and the 4 x 2 x 2
+// accumulators form independent FMA chains.  After the cross-lane
+// reduction every lane holds y[t][0] (row g of tile t) and y[t][1] (row g + 8).
 template <int WT>
-__device__ __forceinline__ void tile_dot(const unsigned char* tile, const __half* xs, int sb0, int sb1, int lane,
-                                      float& y0, float& y1) {
+__device__ __forceinline__ void tiles_dot(const unsigned char* base, uint32_t stride, int T, const __half* xs, int sb0,
+                                          int sb1, int lane, float (&y)[4][2]) {
     constexpr int SK = sb_k<WT>(), XW = SK / 8;  // activation words (half2) per lane per super-block
     const int q = lane & 3;
-    const unsigned char* pa = tile + (lane >> 2) * 64 + q * 16;
+    const unsigned char* pa = base + (lane >> 2) * 64 + q * 16;
     const __half* px = xs + q * (SK / 4);
-    float g0 = 0.f, g1 = 0.f, h0 = 0.f, h1 = 0.f;
-#pragma unroll 2
+    float acc[4][2][2];
+#pragma unroll
+    for (int t = 0; t < 4; t++) acc[t][0][0] = acc[t][0][1] = acc[t][1][0] = acc[t][1][1] = 0.f;
     for (int sb = sb0; sb < sb1; sb++) {
-        const uint4 wg = *reinterpret_cast<const uint4*>(pa + sb * 1024);
-        const uint4 wh = *reinterpret_cast<const uint4*>(pa + sb * 1024 + 512);
         uint32_t xw[XW];
 #pragma unroll
         for (int i = 0; i < XW / 4; i++)
             *reinterpret_cast<uint4*>(xw + 4 * i) = *reinterpret_cast<const uint4*>(px + sb * SK + 8 * i);
-        chunk_fma<WT>(g0, g1, wg, xw);
-        chunk_fma<WT>(h0, h1, wh, xw);
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            if (t < T) {
+                const uint4 wg = *reinterpret_cast<const uint4*>(pa + (size_t)t * stride + sb * 1024);
+                const uint4 wh = *reinterpret_cast<const uint4*>(pa + (size_t)t * stride + sb * 1024 + 512);
+                chunk_fma<WT>(acc[t][0][0], acc[t][0][1], wg, xw);
+                chunk_fma<WT>(acc[t][1][0], acc[t][1][1], wh, xw);
+            }
     }
-    float a = g0 + g1, b = h0 + h1;
-    a += __shfl_xor_sync(0xffffffffu, a, 1);
-    b += __shfl_xor_sync(0xffffffffu, b, 1);
-    a += __shfl_xor_sync(0xffffffffu, a, 2);
-    b += __shfl_xor_sync(0xffffffffu, b, 2);
-    y0 = a;
-    y1 = b;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        float a = acc[t][0][0] + acc[t][0][1], b = acc[t][1][0] + acc[t][1][1];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        b += __shfl_xor_sync(0xffffffffu, b, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        b += __shfl_xor_sync(0xffffffffu, b, 2);
+        y[t][0] = a;
+        y[t][1] = b;
+    }
 }
 
 __host__ __device__ inline int row_bytes(int wtype, int K) {
@@ -583,13 +598,14 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
                 }
                 blocks(OP_O, l, a, b, b - a, src, bys);
             }
-            ctl(OP_OEND, l);
         }
+        ctl(OP_RO, l);
         ctl(OP_GIN, l);
         stream(OP_GU, l, Lw.gu_t, geo.c0, geo.c1, tb_h, kOpRows / 16);
         ctl(OP_ACT, l);
         stream(OP_DN, l, Lw.dn_t, 8 * geo.c0, 8 * geo.c1, rb_h, kMaxCh);  // input-major down rows of the CTA's channels
         ctl(OP_DEND, l);
+        ctl(OP_RD, l);
     }
     if (p.do_lm) {
         ctl(OP_LIN, p.n_layers);
@@ -610,70 +626,83 @@ struct Consumer {
     Sh& sh;
     const unsigned char* ring;
     const Scr& S;
-    uint32_t tag;        // generation tag of this step's LL words and flags
+    uint32_t tag;        // generation + 1 of this step
     long long limit;
     int tid, lane, warp;
-    float4 hres;         // h_mid at outputs 4 tid .. 4 tid + 3 (the down residual of CTA 0)
-    float dacc[4];       // down partial of the same outputs
+    float dacc[4];       // down partial of outputs 4 tid .. 4 tid + 3
     unsigned long long best = 0ull;
 
     __device__ bool abort_seen() const {
         return *(volatile int*)&sh.abort || *(volatile const int*)(p.state + B2_MK_ERR);
     }
-    // Warp 0 polls n per-CTA (or per-unit) flags until every one carries
-    // `want`; the others pass (the vote that follows carries the outcome and,
-    // with the barrier it is, orders their reads after warp 0's acquires).
-    __device__ bool wait_flags(const unsigned* f, int n, unsigned want) const {
-        if (warp != 0) return true;
-        bool ok = true;
-        for (int i = 4 * lane; i < n && ok; i += 128) {
-            for (long long it = 0;; it++) {
-                const uint4 v = ld_acquire_v4(f + i);
-                if ((v.x == want || i >= n) && (v.y == want || i + 1 >= n) && (v.z == want || i + 2 >= n) &&
-                    (v.w == want || i + 3 >= n))
-                    break;
-                if ((it & 63) == 63 && abort_seen()) {
-                    ok = false;
-                    break;
-                }
-                if (it > limit) {
-                    atomicOr(p.state + B2_MK_ERR, 1);
-                    ok = false;
-                    break;
-                }
-                if (it > 8) __nanosleep(32);
+    // Elements 4 tid .. 4 tid + 3 of an LL vector, polled until all carry
+    // tag t (false after the poll limit or an abort elsewhere).
+    __device__ bool poll4(const unsigned long long* src, uint32_t t, float4& v) const {
+        if (4 * tid >= p.hidden) {
+            v = make_float4(0.f, 0.f, 0.f, 0.f);
+            return true;
+        }
+        for (long long it = 0;; it++) {
+            const ulonglong2 a = ll_get2(src + 4 * tid), b = ll_get2(src + 4 * tid + 2);
+            if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t)) {
+                v = make_float4(ll_val(a.x), ll_val(a.y), ll_val(b.x), ll_val(b.y));
+                return true;
             }
+            if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                return false;
+            }
+            if (it > 8) __nanosleep(32);
         }
-        return __all_sync(0xffffffffu, ok);
     }
-    __device__ unsigned* dn_flags(int l) const { return S.fdn + (size_t)l * kMaxG; }
-    __device__ unsigned* ao_flags(int l) const { return S.fao + (size_t)l * kMaxG; }
-    __device__ float* layer_out(int l) const { return S.hacc + ((size_t)l * 2 + (tag & 1)) * kOutCopies * p.hidden; }
-    __device__ float* mid_acc(int l) const { return S.macc + ((size_t)l * 2 + (tag & 1)) * p.hidden; }
+    // One LL word polled until it carries `want`.
+    __device__ bool poll1(const unsigned long long* w, uint32_t want, float& v) const {
+        for (long long it = 0;; it++) {
+            const unsigned long long x = ll_get(w);
+            if (ll_ok(x, want)) {
+                v = ll_val(x);
+                return true;
+            }
+            if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                return false;
+            }
+            if (it > 8) __nanosleep(32);
+        }
+    }
+    // Tag of layer l's words: unique over 2^27 consecutive steps (a word is
+    // rewritten every step, so a reader never meets one older than a step).
+    __device__ uint32_t ltag(int l) const { return tag * (uint32_t)kMaxLayers + (uint32_t)l; }
+    __device__ unsigned long long* opart(int g) const { return S.opart + (size_t)g * p.hidden; }
+    // the kOwn words CTA c sends to reducer r
+    __device__ unsigned long long* dpart(int r, int c) const { return S.dpart + ((size_t)r * kMaxG + c) * kOwn; }
+    // outputs [own0, own0 + nown) this CTA reduces
+    __device__ int own0() const { return kOwn * geo.cta; }
+    __device__ int nown() const { return kOwn * geo.cta < p.hidden ? kOwn : 0; }
 
-    // x at elements 4 tid .. 4 tid + 3: the embedding row (l < 0) or the sum of
-    // the four copies of a layer output written by other CTAs in this launch
-    __device__ float4 load_x(int l) const {
-        const int e = 4 * tid;
-        if (e >= p.hidden) return make_float4(0.f, 0.f, 0.f, 0.f);
+    // x at elements 4 tid .. 4 tid + 3: the embedding row (l < 0) or the
+    // output of layer l
+    __device__ bool load_x(int l, float4& x) const {
         if (l < 0) {
+            const int e = 4 * tid;
+            if (e >= p.hidden) {
+                x = make_float4(0.f, 0.f, 0.f, 0.f);
+                return true;
+            }
             const float* row = p.state[B2_MK_USE_EMB] ? p.staged_emb : p.emb + (size_t)p.state[B2_MK_TOKEN] * p.hidden;
-            return __ldg(reinterpret_cast<const float4*>(row + e));
+            x = __ldg(reinterpret_cast<const float4*>(row + e));
+            return true;
         }
-        const float* src = layer_out(l);
-        float4 a = __ldcg(reinterpret_cast<const float4*>(src + e));
-#pragma unroll
-        for (int c = 1; c < kOutCopies; c++) {
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(src + (size_t)c * p.hidden + e));
-            a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
-        }
-        return a;
+        return poll4(S.xout, ltag(l), x);
     }
 
     // RMSNorm (weights nw) of the distributed vector x (4 elements per
     // thread) and FP16 rounding into dst in the row dots' k order (int8 table
     // for the lm_head: natural order).
-    __device__ bool stage(float4 x, const float* nw, __half* dst, bool perm) {
+    __device__ float4 norm_w(const float* nw) const {
+        return 4 * tid < p.hidden ? __ldg(reinterpret_cast<const float4*>(nw) + tid) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __device__ bool stage(float4 x, float4 w, __half* dst, bool perm) {
         const int e = 4 * tid;
         const bool has = e < p.hidden;
         float ss = has ? fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, x.w * x.w))) : 0.f;
@@ -685,7 +714,6 @@ struct Consumer {
         for (int w = 0; w < NC; w++) t += sh.red[w];
         const float rms = 1.0f / sqrtf(t / (float)p.hidden + p.eps);
         if (has) {
-            const float4 w = __ldg(reinterpret_cast<const float4*>(nw) + tid);
             const float v[4] = {(x.x * rms) * w.x, (x.y * rms) * w.y, (x.z * rms) * w.z, (x.w * rms) * w.w};
 #pragma unroll
             for (int i = 0; i < 4; i++) dst[perm ? stage_pos<WT>(e + i) : e + i] = __float2half_rn(v[i]);
@@ -696,29 +724,46 @@ struct Consumer {
     // ── control operations ──
 
     __device__ bool xin(int l) {
-        bool ok = l == 0 || wait_flags(dn_flags(l - 1), geo.G, tag);
+        const float4 w = norm_w(sh.lay[l].in_norm);  // in flight during the wait
+        float4 x;
+        const bool ok = load_x(l - 1, x);
         if (!vote(ok)) return false;
-        const float4 x = load_x(l - 1);
         if (4 * tid < p.hidden) *reinterpret_cast<float4*>(&sh.xres[4 * tid]) = x;
-        return stage(x, p.layers[l].in_norm, sh.xs[0], true);
+        return stage(x, w, sh.xs[0], true);
     }
 
     // The unit's q heads, new k and v: poll the LL words of head group g, then
     // per-head RMSNorm and RoPE (src/matmul_decoder.c:1495-1510); unit r = 0
     // appends K and V at this position (:1512-1516).
     __device__ bool ain(int l, int g, int r) {
-        const B2MkLayer& Lw = p.layers[l];
-        const unsigned long long* qkv = S.qkv + (size_t)l * geo.nqkv;
+        const B2MkLayer& Lw = sh.lay[l];
+        const unsigned long long* qkv = S.qkv;
+        const uint32_t t = ltag(l);
         const int h = warp, e0 = lane * 4;
         bool ok = true;
         float x[4] = {0.f, 0.f, 0.f, 0.f};
+        // static inputs first, in flight during the poll: norm weights, RoPE angles
+        const float* nwp = h < kGq ? Lw.q_norm : h == kGq ? Lw.k_norm : nullptr;
+        const float4 nw = nwp ? __ldg(reinterpret_cast<const float4*>(nwp + e0)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        float cs[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+        if (h <= kGq) {
+            const float* ct = p.cos_tab + (size_t)geo.pos * (kHD / 2);
+            const float* st = p.sin_tab + (size_t)geo.pos * (kHD / 2);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                // interleaved pairs (2i, 2i+1) use angle i; split halves (e, e + hd/2) use angle e
+                const int i = p.rope_style == 0 ? (e0 + j) >> 1 : (lane < 16 ? e0 + j : e0 + j - kHD / 2);
+                cs[j] = __ldg(ct + i);
+                sn[j] = __ldg(st + i);
+            }
+        }
         if (h < kGq + 2) {
             const unsigned long long* src = h < kGq ? qkv + (size_t)(g * kGq + h) * kHD
                                             : h == kGq ? qkv + geo.qd + (size_t)g * kHD
                                                        : qkv + geo.qd + geo.kvd + (size_t)g * kHD;
             for (long long it = 0;; it++) {
                 const ulonglong2 a = ll_get2(src + e0), b = ll_get2(src + e0 + 2);
-                if (ll_ok(a.x, tag) && ll_ok(a.y, tag) && ll_ok(b.x, tag) && ll_ok(b.y, tag)) {
+                if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t)) {
                     x[0] = ll_val(a.x), x[1] = ll_val(a.y), x[2] = ll_val(b.x), x[3] = ll_val(b.y);
                     break;
                 }
@@ -732,32 +777,25 @@ struct Consumer {
         }
         if (!vote(ok)) return false;
         if (h <= kGq) {
-            const float* nwp = h < kGq ? Lw.q_norm : Lw.k_norm;
             if (nwp) {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(nwp + e0));
                 float ss = fmaf(x[0], x[0], fmaf(x[1], x[1], fmaf(x[2], x[2], x[3] * x[3])));
                 ss = b2::warp_sum(ss);
                 const float rms = 1.0f / sqrtf(ss / (float)kHD + p.eps);
-                x[0] = (x[0] * rms) * w.x, x[1] = (x[1] * rms) * w.y, x[2] = (x[2] * rms) * w.z,
-                x[3] = (x[3] * rms) * w.w;
+                x[0] = (x[0] * rms) * nw.x, x[1] = (x[1] * rms) * nw.y, x[2] = (x[2] * rms) * nw.z,
+                x[3] = (x[3] * rms) * nw.w;
             }
-            const float* ct = p.cos_tab + (size_t)geo.pos * (kHD / 2);
-            const float* st = p.sin_tab + (size_t)geo.pos * (kHD / 2);
             if (p.rope_style == 0) {  // interleaved pairs (2i, 2i+1) at angle i
 #pragma unroll
                 for (int j = 0; j < 4; j += 2) {
-                    const float c = __ldg(ct + (e0 + j) / 2), s = __ldg(st + (e0 + j) / 2);
                     const float x0 = x[j], x1 = x[j + 1];
-                    x[j] = x0 * c - x1 * s;
-                    x[j + 1] = x1 * c + x0 * s;
+                    x[j] = x0 * cs[j] - x1 * sn[j];
+                    x[j + 1] = x1 * cs[j] + x0 * sn[j];
                 }
             } else {  // split halves (e, e + hd/2) at angle e
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const int i = lane < 16 ? e0 + j : e0 + j - kHD / 2;
-                    const float c = __ldg(ct + i), s = __ldg(st + i);
                     const float other = __shfl_xor_sync(0xffffffffu, x[j], 16);
-                    x[j] = lane < 16 ? x[j] * c - other * s : x[j] * c + other * s;
+                    x[j] = lane < 16 ? x[j] * cs[j] - other * sn[j] : x[j] * cs[j] + other * sn[j];
                 }
             }
         }
@@ -816,48 +854,137 @@ struct Consumer {
     }
 
     __device__ bool gin(int l) {
-        bool ok = wait_flags(ao_flags(l), geo.units, tag);
-        if (!vote(ok)) return false;
-        const int e = 4 * tid;
-        hres = e < p.hidden ? __ldcg(reinterpret_cast<const float4*>(mid_acc(l) + e)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 w = norm_w(sh.lay[l].post_norm);
+        float4 h;
+        const bool ok = poll4(S.hmid, ltag(l), h);
+        if (!vote(ok)) return false;  // (also: every RO of this CTA read xres as x)
+        if (4 * tid < p.hidden) *reinterpret_cast<float4*>(&sh.xres[4 * tid]) = h;  // the residual of RD
 #pragma unroll
         for (int i = 0; i < 4; i++) dacc[i] = 0.f;
-        return stage(hres, p.layers[l].post_norm, sh.xs[1], true);
+        return stage(h, w, sh.xs[1], true);
     }
 
+    // h_mid of the outputs this CTA owns: the nkv o_proj partials (fixed
+    // order) plus the residual x.
+    __device__ bool ro(int l) {
+        const int o0 = own0(), n = nown();
+        float* red = &sh.mrg_o[0][0][0];  // [nkv][kOwn] (free outside attention)
+        bool ok = true;
+        if (tid < n * p.nkv) {  // every partial polled at once, one per thread
+            const int g = tid / n, j = tid - g * n;
+            float v;
+            ok = poll1(opart(g) + o0 + j, ltag(l), v);
+            red[g * kOwn + j] = v;
+        }
+        if (!vote(ok)) return false;
+        if (tid < n) {
+            float acc = 0.f;
+            for (int g = 0; g < p.nkv; g++) acc += red[g * kOwn + tid];
+            ll_put(S.hmid + o0 + tid, acc + sh.xres[o0 + tid], ltag(l));
+        }
+        return vote(true);  // the partials are read before the next use of mrg_o
+    }
+
+    // Layer output of the outputs this CTA owns: every CTA's down partial
+    // (summed in CTA order) plus the residual h_mid.  The partials are polled
+    // only once the publication counter says all CTAs have sent theirs, which
+    // keeps early reducers from loading L2 while the last CTAs still stream
+    // their down weights; the tags still decide what is read.
+    __device__ bool rd(int l) {
+        const int o0 = own0(), n = nown();
+        if (n == 0) return true;
+        float* red = &sh.mrg_o[0][0][0];  // [kMaxG][kOwn] partial sums by source CTA (free here)
+        bool ok = true;
+        if (tid == 0) {
+            const unsigned long long target =
+                ((unsigned long long)(tag - 1) * p.n_layers + l + 1) * (unsigned long long)geo.G;
+            for (long long it = 0;; it++) {
+                unsigned long long c;
+                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(c) : "l"(S.dcnt) : "memory");
+                if (c >= target) break;
+                if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                    if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                    ok = false;
+                    break;
+                }
+                if (it > 8) __nanosleep(32);
+            }
+        }
+        if (!vote(ok)) return false;
+        const uint32_t t = ltag(l);
+        for (int c = tid; c < geo.G && ok; c += kCons) {
+            const unsigned long long* src = dpart(geo.cta, c);
+            for (long long it = 0;; it++) {
+                const ulonglong2 a = ll_get2(src), b = ll_get2(src + 2), e = ll_get2(src + 4), f = ll_get2(src + 6);
+                if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t) && ll_ok(e.x, t) &&
+                    ll_ok(e.y, t) && ll_ok(f.x, t) && ll_ok(f.y, t)) {
+                    float4* dst = reinterpret_cast<float4*>(red + c * kOwn);
+                    dst[0] = make_float4(ll_val(a.x), ll_val(a.y), ll_val(b.x), ll_val(b.y));
+                    dst[1] = make_float4(ll_val(e.x), ll_val(e.y), ll_val(f.x), ll_val(f.y));
+                    break;
+                }
+                if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                    if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                    ok = false;
+                    break;
+                }
+                if (it > 8) __nanosleep(32);
+            }
+        }
+        if (!vote(ok)) return false;
+        if (tid < n) {
+            float acc = 0.f;
+            for (int c = 0; c < geo.G; c++) acc += red[c * kOwn + tid];
+            ll_put(S.xout + o0 + tid, acc + sh.xres[o0 + tid], t);
+        }
+        return vote(true);  // the partial area is read before the next use of mrg_o
+    }
+
+    // This CTA's down partial (its channels' contribution to every output,
+    // times the per-output scale) as LL words for the reducers.
     __device__ bool dend(int l) {
         const int n = 4 * tid;
         if (n < p.hidden) {
-            const float* ds = p.layers[l].dn_s;
+            const float* ds = sh.lay[l].dn_s;
             float4 d = make_float4(dacc[0], dacc[1], dacc[2], dacc[3]);
             if (ds) {
                 const float4 sc = __ldg(reinterpret_cast<const float4*>(ds + n));
                 d.x *= sc.x, d.y *= sc.y, d.z *= sc.z, d.w *= sc.w;
             }
-            if (geo.cta == 0) d.x += hres.x, d.y += hres.y, d.z += hres.z, d.w += hres.w;
-            red_add_v4(layer_out(l) + (size_t)(geo.cta % kOutCopies) * p.hidden + n, d);
+            // outputs n .. n + 3 are half (tid & 1) of reducer tid / 2's words
+            unsigned long long* dst = dpart(tid >> 1, geo.cta) + 4 * (tid & 1);
+            const unsigned long long t = (unsigned long long)ltag(l) << 32;
+            const ulonglong2 a = make_ulonglong2(t | __float_as_uint(d.x), t | __float_as_uint(d.y));
+            const ulonglong2 b = make_ulonglong2(t | __float_as_uint(d.z), t | __float_as_uint(d.w));
+            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a.x), "l"(a.y) : "memory");
+            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(b.x), "l"(b.y) : "memory");
         }
-        if (!vote(true)) return false;  // every consumer's additions precede the release
-        if (tid == 0) st_release_u32(dn_flags(l) + geo.cta, tag);
+        // count this CTA's publication (a hint for the reducers' polling: the
+        // other warps' words may still be in flight, their tags decide)
+        if (tid == 0) asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(S.dcnt) : "memory");
         return true;
     }
 
     __device__ bool lin() {
-        bool ok = wait_flags(dn_flags(p.n_layers - 1), geo.G, tag + (p.stall_test ? 1u : 0u));
+        const float4 w = norm_w(p.final_norm);
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool ok = true;
+        if (p.stall_test) {  // a word no CTA writes with this tag: the wait runs out
+            float v;
+            ok = poll1(S.xout, ltag(p.n_layers), v);  // (the next layer's tag: never written)
+        }
+        ok = ok && load_x(p.n_layers - 1, x);
         if (!vote(ok)) return false;
-        const float4 x = load_x(p.n_layers - 1);
         if (geo.cta == 0 && 4 * tid < p.hidden) reinterpret_cast<float4*>(S.hfinal)[tid] = x;
         best = 0ull;
-        return stage(x, p.final_norm, sh.xs[0], false);  // int8 table: natural k order
+        return stage(x, w, sh.xs[0], false);  // int8 table: natural k order
     }
 
     __device__ bool pfin() {  // prefill-mode step: publish the final hidden state
-        bool ok = geo.cta != 0 || wait_flags(dn_flags(p.n_layers - 1), geo.G, tag);
+        float4 x;
+        const bool ok = geo.cta != 0 || load_x(p.n_layers - 1, x);
         if (!vote(ok)) return false;
-        if (geo.cta == 0) {
-            const float4 x = load_x(p.n_layers - 1);
-            if (4 * tid < p.hidden) reinterpret_cast<float4*>(S.hfinal)[tid] = x;
-        }
+        if (geo.cta == 0 && 4 * tid < p.hidden) reinterpret_cast<float4*>(S.hfinal)[tid] = x;
         return true;
     }
 
@@ -883,17 +1010,16 @@ struct Consumer {
                              int pb, bool& ok) {
         const int s0 = split_lo(nsb, NC, warp), s1 = split_lo(nsb, NC, warp + 1);
         const int g = lane >> 2;
-        for (int t = 0; t < T; t++) {
-            float y0 = 0.f, y1 = 0.f;
-            if (s1 > s0) {
-                if (int8) tile_dot<B2_W_I8>(buf + (size_t)t * stride, xs, s0, s1, lane, y0, y1);
-                else tile_dot<WT>(buf + (size_t)t * stride, xs, s0, s1, lane, y0, y1);
-            }
-            if ((lane & 3) == 0) {
-                sh.part[pb][warp][16 * t + g] = y0;
-                sh.part[pb][warp][16 * t + g + 8] = y1;
-            }
-        }
+        float y[4][2];
+        if (int8) tiles_dot<B2_W_I8>(buf, stride, T, xs, s0, s1, lane, y);
+        else tiles_dot<WT>(buf, stride, T, xs, s0, s1, lane, y);
+        if ((lane & 3) == 0)
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+                if (t < T) {
+                    sh.part[pb][warp][16 * t + g] = y[t][0];
+                    sh.part[pb][warp][16 * t + g + 8] = y[t][1];
+                }
         ok = vote(true);
         float v = 0.f;
         if (ok && tid < 16 * T)
@@ -905,11 +1031,11 @@ struct Consumer {
     __device__ bool qkv_tiles(const Desc& d, const unsigned char* buf, int pb) {
         const int T = d.b - d.a, nsb = row_bytes(WT, p.hidden) / 64;
         const int r = 16 * d.a + tid;
-        const float* sc = p.layers[d.l].qkv_s;
+        const float* sc = sh.lay[d.l].qkv_s;
         const float s = (sc && tid < 16 * T) ? __ldg(sc + r) : 1.f;
         bool ok;
         const float v = op_dots(buf, 16u * row_bytes(WT, p.hidden), T, nsb, sh.xs[0], false, pb, ok);
-        if (ok && tid < 16 * T) ll_put(S.qkv + (size_t)d.l * geo.nqkv + r, v * s, tag);
+        if (ok && tid < 16 * T) ll_put(S.qkv + r, v * s, ltag(d.l));
         return ok;
     }
 
@@ -921,11 +1047,11 @@ struct Consumer {
     __device__ bool o_tiles(const Desc& d, const unsigned char* buf, int pb) {
         const int T = d.b - d.a, nsb = row_bytes(WT, kGq * kHD) / 64;
         const int r = 16 * d.a + tid;
-        const float* sc = p.layers[d.l].o_s;
+        const float* sc = sh.lay[d.l].o_s;
         const float s = (sc && tid < 16 * T) ? __ldg(sc + r) : 1.f;
         bool ok;
         const float v = op_dots(buf, 1024u * (uint32_t)nsb, T, nsb, sh.xo, false, pb, ok);
-        if (ok && tid < 16 * T) red_add(mid_acc(d.l) + r, v * s + (d.c == 0 ? sh.xres[r] : 0.f));  // residual once per row
+        if (ok && tid < 16 * T) ll_put(opart(d.c) + r, v * s, ltag(d.l));
         return ok;
     }
 
@@ -933,7 +1059,7 @@ struct Consumer {
     // gets channel j's SiLU(gate) * up, FP16-rounded as the down input.
     __device__ bool gu_tiles(const Desc& d, const unsigned char* buf, int pb) {
         const int T = d.b - d.a, nsb = row_bytes(WT, p.hidden) / 64;
-        const float* sc = p.layers[d.l].gu_ts;
+        const float* sc = sh.lay[d.l].gu_ts;
         const float s = (sc && tid < 16 * T) ? __ldg(sc + 16 * d.a + tid) : 1.f;
         bool ok;
         const float v = op_dots(buf, 16u * row_bytes(WT, p.hidden), T, nsb, sh.xs[1], false, pb, ok) * s;
@@ -1018,15 +1144,13 @@ struct Consumer {
                 case OP_KV: kv_op(d, buf); break;
                 case OP_AOUT: ok = vote(true) && aout(); break;
                 case OP_O: ok = o_tiles(d, buf, pb ^= 1); break;
-                case OP_OEND:
-                    ok = vote(true);
-                    if (ok && tid == 0) st_release_u32(ao_flags(d.l) + geo.cta, tag);
-                    break;
+                case OP_RO: ok = vote(true) && ro(d.l); break;
                 case OP_GIN: ok = gin(d.l); break;
                 case OP_GU: ok = gu_tiles(d, buf, pb ^= 1); break;
                 case OP_ACT: ok = vote(true); break;
                 case OP_DN: dn_rows(d, buf); break;
                 case OP_DEND: ok = vote(true) && dend(d.l); break;
+                case OP_RD: ok = vote(true) && rd(d.l); break;
                 case OP_LIN: ok = lin(); break;
                 case OP_LM: ok = lm_tiles(d, buf, pb ^= 1); break;
                 case OP_LEND: ok = vote(true) && lend(); break;
@@ -1067,26 +1191,15 @@ __global__ void __launch_bounds__(kThreads, 1) mk2_kernel(const __grid_constant_
     __syncthreads();
 
     const Geo geo = make_geo(p);
-    const Scr S = scr_layout(p.scratch, p.n_layers, p.hidden, geo.nqkv, nullptr);
+    const Scr S = scr_layout(p.scratch, p.n_layers, p.hidden, geo.nqkv, p.nkv, nullptr);
     const unsigned long long gen = (unsigned long long)(unsigned)p.state[B2_MK_GEN];
 
     if (warp == NC) {
         if (lane == 0) produce<WT>(p, geo, sh, ring, limit);
     } else {
-        {  // zero this CTA's slice of the next step's accumulators (the other parity)
-            const int per = p.hidden / 4;
-            const unsigned npar = (unsigned)(gen + 2) & 1u;
-            float4* z = reinterpret_cast<float4*>(S.hacc);
-            const int th = p.n_layers * kOutCopies * per;
-            for (int i = split_lo(th, geo.G, geo.cta) + tid; i < split_lo(th, geo.G, geo.cta + 1); i += kCons) {
-                const int l = i / (kOutCopies * per), rest = i % (kOutCopies * per);
-                z[((size_t)l * 2 + npar) * kOutCopies * per + rest] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            float4* zm = reinterpret_cast<float4*>(S.macc);
-            const int tm = p.n_layers * per;
-            for (int i = split_lo(tm, geo.G, geo.cta) + tid; i < split_lo(tm, geo.G, geo.cta + 1); i += kCons)
-                zm[((size_t)(i / per) * 2 + npar) * per + (i % per)] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        for (int i = tid; i < p.n_layers * (int)(sizeof(B2MkLayer) / 8); i += kCons)
+            reinterpret_cast<unsigned long long*>(sh.lay)[i] = reinterpret_cast<const unsigned long long*>(p.layers)[i];
+        consumer_sync();
         Consumer<WT> cons{p, geo, sh, ring, S, (uint32_t)(gen + 1), limit, tid, lane, warp};
         if (cons.run()) {  // FIN: the last CTA to arrive publishes the step
             consumer_sync();
@@ -1168,6 +1281,8 @@ int launch(const B2MkPlan* p, cudaStream_t s) {
     B2_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     if (sms < p->nkv || sms > kMaxG)
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_mk2_decode: %d SMs (kv heads %d, at most %d SMs)", sms, p->nkv, kMaxG);
+    if ((p->hidden + kOwn - 1) / kOwn > sms)
+        return b2_set_error(B2_ERR_INVALID_ARG, "b2_mk2_decode: hidden %d needs more SMs", p->hidden);
     if (8 * ((p->ffn / 8 + sms - 1) / sms) > kMaxCh)
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_mk2_decode: ffn %d needs more SMs", p->ffn);
     cudaLaunchConfig_t cfg = {};
@@ -1192,18 +1307,18 @@ extern "C" int b2_mk2_max_context(void) { return kFuseMax; }
 extern "C" size_t b2_mk2_scratch_bytes(int n_layers, int hidden, int ffn, int nq, int nkv, int hd) {
     (void)ffn;
     size_t total = 0;
-    scr_layout(nullptr, n_layers, hidden, nq * hd + 2 * nkv * hd, &total);
+    scr_layout(nullptr, n_layers, hidden, nq * hd + 2 * nkv * hd, nkv, &total);
     return total;
 }
 
 extern "C" float* b2_mk2_final_hidden(const B2MkPlan* p) {
-    Scr s = scr_layout(p->scratch, p->n_layers, p->hidden, p->nq * p->hd + 2 * p->nkv * p->hd, nullptr);
+    Scr s = scr_layout(p->scratch, p->n_layers, p->hidden, p->nq * p->hd + 2 * p->nkv * p->hd, p->nkv, nullptr);
     return s.hfinal;
 }
 
 extern "C" int b2_mk2_check(const B2MkPlan* p) {
     if (!p) return B2_ERR_INVALID_ARG;
-    if (p->n_layers < 1 || p->n_layers > B2_MK_MAX_LAYERS || p->hd != kHD || p->nkv < 1 || p->nq != kGq * p->nkv)
+    if (p->n_layers < 1 || p->n_layers > kMaxLayers || p->hd != kHD || p->nkv < 1 || p->nq != kGq * p->nkv)
         return B2_ERR_INVALID_ARG;
     // every matmul a whole number of 16-row tiles of 64-byte super-blocks
     if (p->hidden != kMaxH || p->ffn % 8 || p->ffn > kMaxF || p->vocab % 16 || (p->nq * kHD + 2 * p->nkv * kHD) % 16)

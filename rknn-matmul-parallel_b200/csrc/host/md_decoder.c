@@ -74,6 +74,10 @@ struct MatmulDecoderContext {
     void* mk2_buf;    /* tile-major weights, lm_head tiles, scratch and state (one allocation) */
     int test_hooks;   /* B2_MK_POLL_LIMIT was set at create: B2_MK_STALL_TEST is read per step */
     size_t mk2_scratch_bytes;
+    /* on-device sampling: draw i of this context uses (sample_seed, sample_counter = i) */
+    unsigned long long sample_seed, sample_counter;
+    int* d_sample;    /* [8]: [0] token, [1..4] sampler info, then the repeat list */
+    int d_sample_cap; /* repeat-list entries d_sample has room for */
     b2_event_t ev[3];
     MatmulDecoderStats stats;
 };
@@ -334,6 +338,8 @@ static MatmulDecoderContext* ctx_finish(MatmulDecoderContext* ctx) {
     mk_setup(ctx);
     mk2_setup(ctx);
     ctx->config = ctx->model.cfg;
+    /* the draws follow the C library's generator, as the host sampler does */
+    ctx->sample_seed = ((unsigned long long)(unsigned)rand() << 32) ^ (unsigned long long)(unsigned)rand();
     printf("[MatmulDecoder] Ready: %d layers, hidden=%d, heads=%d/%d, ffn=%d, vocab=%d, quant=%d, "
            "max_seq=%d, arena %.1f MB, decode kernel: %s\n",
            ctx->config.num_layers, ctx->config.hidden_dim, ctx->config.num_q_heads,
@@ -429,6 +435,7 @@ void matmul_decoder_destroy(MatmulDecoderContext* ctx) {
     b2_host_free(ctx->h_mk_state);
     b2_host_free(ctx->h_mk2_state);
     if (ctx->mk2_buf) b2_free(ctx->mk2_buf);
+    if (ctx->d_sample) b2_free(ctx->d_sample);
     md_model_free(&ctx->model);
     free(ctx);
 }
@@ -648,6 +655,47 @@ int matmul_decoder_step_get_logits(MatmulDecoderContext* ctx, int token_id, cons
 
 int matmul_decoder_step_token(MatmulDecoderContext* ctx, int token_id, const float* embedding) {
     return step_impl(ctx, token_id, embedding, 1, NULL);
+}
+
+int matmul_decoder_set_seed(MatmulDecoderContext* ctx, unsigned long long seed) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    ctx->sample_seed = seed;
+    ctx->sample_counter = 0;
+    return MATMUL_DECODER_OK;
+}
+
+/* One step whose logits stay on the device, then b2_sample_token on the same
+ * stream: only the token crosses to the host. */
+int matmul_decoder_step_sample(MatmulDecoderContext* ctx, int token_id, const float* embedding,
+                               const SamplingParams* params) {
+    if (!ctx) return MATMUL_DECODER_ERR_INVALID_ARG;
+    const SamplingParams p = params ? *params : sampling_params_greedy();
+    const int penalize = p.repeat_penalty != 1.0f && p.repeat_tokens && p.n_repeat_tokens > 0;
+    if (p.n_repeat_tokens < 0 || (penalize && !(p.repeat_penalty > 0.f))) return MATMUL_DECODER_ERR_INVALID_ARG;
+    if (p.top_k == 1 && !penalize) return step_impl(ctx, token_id, embedding, 1, NULL);
+    const int n_rep = penalize ? p.n_repeat_tokens : 0;
+    b2_set_device(ctx->device);
+    int rc = 0;
+    if (!ctx->d_sample || ctx->d_sample_cap < n_rep) {
+        if (ctx->d_sample) b2_free(ctx->d_sample);
+        ctx->d_sample = NULL;
+        const int cap = n_rep > 256 ? n_rep : 256;
+        if ((rc = b2_malloc((void**)&ctx->d_sample, (size_t)(8 + cap) * 4))) return fail("sampler buffer", rc);
+        ctx->d_sample_cap = cap;
+    }
+    const int r = step_impl(ctx, token_id, embedding, 1, NULL);
+    if (r < 0) return r;
+    b2_stream_t s = ctx->stream;
+    if (n_rep && (rc = b2_memcpy_h2d(ctx->d_sample + 8, p.repeat_tokens, (size_t)n_rep * 4, s)))
+        return fail("repeat list copy", rc);
+    rc = b2_sample_token(ctx->logits, ctx->model.cfg.vocab_size, ctx->d_sample + 8, n_rep,
+                         penalize ? p.repeat_penalty : 1.0f, p.top_k, p.top_p, p.temperature, ctx->sample_seed,
+                         ctx->sample_counter, ctx->d_sample, ctx->d_sample + 1, s);
+    if (!rc) rc = b2_memcpy_d2h(ctx->h_tok, ctx->d_sample, 4, s);
+    if (!rc) rc = b2_stream_sync(s);
+    if (rc) return fail("on-device sampling", rc);
+    ctx->sample_counter++;
+    return ctx->h_tok[0];
 }
 
 int matmul_decoder_step_head(MatmulDecoderContext* ctx, int token_id, const float* embedding,

@@ -107,34 +107,21 @@ int matmul_decoder_generate(MatmulDecoderContext* ctx, const int* prompt_tokens,
                             int max_new_tokens, SamplingParams* params, GenerateCallback callback,
                             void* user_data) {
     if (!ctx || !prompt_tokens || n_prompt <= 0 || max_new_tokens < 0) return MATMUL_DECODER_ERR_INVALID_ARG;
-    const MatmulDecoderConfig* c = matmul_decoder_get_config(ctx);
-    const int greedy = !params || (params->top_k == 1 && (params->repeat_penalty == 1.0f ||
-                                                          !params->repeat_tokens));
     for (int i = 0; i < n_prompt - 1; i++) {
         int rc = matmul_decoder_step(ctx, prompt_tokens[i], NULL, NULL);
         if (rc < 0) return rc;
     }
     if (max_new_tokens == 0) return 0;
-    float* logits = greedy ? NULL : (float*)malloc((size_t)c->vocab_size * sizeof(float));
-    if (!greedy && !logits) return MATMUL_DECODER_ERR_MEMORY;
+    /* every produced token is drawn on the device (greedy steps run the
+     * argmax there): no logits are copied to the host */
     int tok = prompt_tokens[n_prompt - 1], produced = 0;
     for (int i = 0; i < max_new_tokens; i++) {
-        int next;
-        if (greedy) {
-            next = matmul_decoder_step_token(ctx, tok, NULL);
-        } else {
-            next = matmul_decoder_step(ctx, tok, NULL, logits);
-            if (next >= 0) next = matmul_sample_token(logits, c->vocab_size, params);
-        }
-        if (next < 0) {
-            free(logits);
-            return produced > 0 ? produced : next;
-        }
+        const int next = matmul_decoder_step_sample(ctx, tok, NULL, params);
+        if (next < 0) return produced > 0 ? produced : next;
         produced++;
         if (callback) callback(next, NULL, user_data);
         tok = next;
     }
-    free(logits);
     return produced;
 }
 

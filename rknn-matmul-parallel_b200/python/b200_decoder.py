@@ -59,6 +59,12 @@ class B2GemvArgs(ctypes.Structure):
                 ("norm_w", c_vp), ("eps", c_float), ("epilogue", c_int)]
 
 
+class SamplingParams(ctypes.Structure):
+    """SamplingParams of include/matmul_decoder.h (the reference's layout)."""
+    _fields_ = [("top_k", c_int), ("top_p", ctypes.c_float), ("temperature", ctypes.c_float),
+                ("repeat_penalty", ctypes.c_float), ("repeat_tokens", c_vp), ("n_repeat_tokens", c_int)]
+
+
 class B2GemmArgs(ctypes.Structure):
     _fields_ = [("y", c_vp), ("ldy", c_int), ("x16", c_vp), ("ldx", c_int), ("M", c_int),
                 ("K", c_int), ("N", c_int), ("w", c_vp), ("scales", c_vp), ("wtype", c_int),
@@ -97,6 +103,8 @@ SIGNATURES = {
     "matmul_decoder_export_hf_model": (c_int, [ctypes.c_char_p, ctypes.c_char_p, c_int]),
     "matmul_decoder_step_token": (c_int, [c_vp, c_int, c_vp]),
     "matmul_decoder_decode_greedy": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    "matmul_decoder_step_sample": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "matmul_decoder_set_seed": (c_int, [c_vp, ctypes.c_ulonglong]),
     "matmul_decoder_set_kv": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_get_kv": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_set_seq_len": (c_int, [c_vp, c_int]),
@@ -115,6 +123,9 @@ SIGNATURES = {
     "matmul_decoder_batch_shard_vocab": (c_int, [c_vp, c_int, c_int, c_vp, c_int]),
     # b2_kernels.h
     "b2_last_error": (ctypes.c_char_p, []),
+    "b2_sample_max_vocab": (c_size, []),
+    "b2_sample_token": (c_int, [c_vp, c_int, c_vp, c_int, ctypes.c_float, c_int, ctypes.c_float, ctypes.c_float,
+                                ctypes.c_ulonglong, ctypes.c_ulonglong, c_vp, c_vp, c_vp]),
     "b2_device_count": (c_int, [c_vp]),
     "b2_set_device": (c_int, [c_int]),
     "b2_get_device": (c_int, [c_vp]),
@@ -299,6 +310,18 @@ class Decoder:
     def step_token(self, token_id=-1, embedding=None):
         emb = None if embedding is None else np.ascontiguousarray(embedding, np.float32)
         return capi().matmul_decoder_step_token(self.ctx, token_id, _ptr(emb))
+
+    def step_sample(self, token_id=-1, params=None, embedding=None):
+        """matmul_decoder_step_sample: the step's token drawn on the device."""
+        emb = None if embedding is None else np.ascontiguousarray(embedding, np.float32)
+        keep = params  # the repeat list stays alive for the call
+        tok = capi().matmul_decoder_step_sample(self.ctx, token_id, _ptr(emb),
+                                                ctypes.byref(params) if params is not None else None)
+        del keep
+        return tok
+
+    def set_seed(self, seed):
+        check(capi().matmul_decoder_set_seed(self.ctx, seed), "set_seed")
 
     def decode_greedy(self, first_token, n_tokens):
         """Device-resident greedy loop; returns (tokens, device_ms)."""
