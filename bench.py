@@ -358,11 +358,17 @@ def measure_single_stream(args, world, rank, local, workload, context, steps, wa
         if tok < 0:
             raise RuntimeError(f"step_token failed ({tok})")
     e_s = max_over_ranks(world, time.perf_counter() - e0)
-    persistent = dec.uses_persistent_kernel() and ctx0 + steps <= 2048
+    kinds = {dec.step_kernel(ctx0), dec.step_kernel(ctx0 + steps - 1)}
+    persistent = kinds.pop() if len(kinds) == 1 else -1  # -1: the run crossed a routing boundary
     dec.close()
     attended = ctx0 + (steps + 1) / 2.0
     return {"quant": quant, "mdir": mdir, "ctx0": ctx0, "ms": ms, "e2e_s": e_s, "clocks": clk,
             "toks": toks, "bytes": token_bytes(shape, quant, attended), "persistent": persistent}
+
+
+KERNEL_NAMES = {2: "tile-stream persistent kernel b2_mk2_decode (mk2_kernel), one launch per token",
+                1: "persistent kernel b2_mk_decode, one launch per token",
+                0: "CUDA graph of per-op kernels"}
 
 
 def decode_roofline(m: dict, steps: int, peaks: dict, traffic=None) -> dict:
@@ -371,8 +377,7 @@ def decode_roofline(m: dict, steps: int, peaks: dict, traffic=None) -> dict:
     achieved = m["bytes"] / (ms_tok * 1e-3) / 1e9
     r = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
          "frac": round(achieved / peak, 4), "traffic": traffic,
-         "kernel": "whole decode step (" + ("persistent kernel b2_mk_decode, one launch per token" if m["persistent"]
-                                            else "CUDA graph of per-op kernels") + ")",
+         "kernel": "whole decode step (" + KERNEL_NAMES.get(m["persistent"], "mixed routing") + ")",
          "bytes_per_token": int(m["bytes"]),
          "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured, of measured)" if peaks else "fallback 6.65 TB/s"}
     return r

@@ -347,6 +347,12 @@ int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out);
  * cover). */
 int matmul_decoder_uses_persistent_kernel(const MatmulDecoderContext* ctx);
 
+/* ADDITIVE.  Which kernel a single-token step with n_cached positions already
+ * in the cache runs: 2 = the tile-stream persistent kernel (b2_mk2_decode),
+ * 1 = the first persistent kernel (b2_mk_decode), 0 = the CUDA graph of
+ * per-op kernels. */
+int matmul_decoder_step_kernel(const MatmulDecoderContext* ctx, int n_cached);
+
 /* ADDITIVE.  Quantize one FP16 [K][N] weight on the host into the on-disk
  * quantized layout: bits = 8 writes int8 [K][N]; bits = 4 writes int4 [K][N/2]
  * (low nibble = even column).  scales_out gets FP32 [N].  Bit-exact with the

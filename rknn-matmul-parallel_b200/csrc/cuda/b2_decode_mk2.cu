@@ -67,19 +67,19 @@ constexpr int kGq = 2;                 // q heads per kv head
 constexpr int kND = 64;                // operation slots
 constexpr int kOpMax = 64 * 1024;      // bytes of one data operation
 constexpr int kOpRows = 64;            // rows (4 tiles) of one dot operation
-constexpr int kKVPos = 64;             // cached positions per K/V operation
+constexpr int kKVPos = 128;            // cached positions per K/V operation (K and V: 64 KB)
+constexpr int kSplit = 8;              // units of a kv head that share its positions above 2 kKVPos
 constexpr int kMaxH = 4 * kCons;       // hidden: one float4 per consumer thread
 constexpr int kMaxF = 3072;            // longest staged activation
 constexpr int kMaxCh = 32;             // gate|up channels per CTA
 constexpr int kOwn = 8;                // outputs each reducer CTA owns (CTAs 0 .. hidden / 8 - 1)
-constexpr int kFuseMax = 512;          // cached positions the host routes here
 constexpr int kMaxG = 256;             // CTAs the partial arrays have room for
 constexpr int kMaxLayers = 32;         // layers of the shared-memory pointer table
 constexpr long long kDefaultPolls = 1ll << 22;
 static_assert(kCons == kGq * kHD, "the attention merge gives one consumer thread per (q head, dim)");
 
 enum Op : int {
-    OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_O, OP_RO, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND, OP_RD,
+    OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_APUB, OP_AMRG, OP_O, OP_RO, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND, OP_RD,
     OP_LIN, OP_LM, OP_LEND, OP_PFIN, OP_DONE
 };
 
@@ -130,6 +130,7 @@ static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB per-
 struct Scr {
     unsigned long long* cnt;   // [8]: [0] CTAs finished, [1] best key
     unsigned long long* qkv;   // LL [nqkv]
+    unsigned long long* apart; // LL [nkv][kSplit][4 + 2 hd] attention partials: m, l per q head, then o
     unsigned long long* opart; // LL [nkv][H] o_proj partials, one per kv head
     unsigned long long* hmid;  // LL [H] h_mid = x + o_proj(attention)
     unsigned long long* dpart; // LL [H / kOwn][kMaxG][kOwn] down partials by reducer, then source CTA
@@ -152,6 +153,7 @@ __host__ __device__ inline Scr scr_layout(void* base, int L, int H, int nqkv, in
     s.cnt = reinterpret_cast<unsigned long long*>(take(8 * 8));
     (void)L;
     s.qkv = reinterpret_cast<unsigned long long*>(take((size_t)nqkv * 8));
+    s.apart = reinterpret_cast<unsigned long long*>(take((size_t)nkv * kSplit * (4 + 2 * kHD) * 8));
     s.opart = reinterpret_cast<unsigned long long*>(take((size_t)nkv * H * 8));
     s.hmid = reinterpret_cast<unsigned long long*>(take((size_t)H * 8));
     s.dpart = reinterpret_cast<unsigned long long*>(take((size_t)kMaxG * H * 8));
@@ -445,6 +447,7 @@ __device__ __forceinline__ void attend8(Sh& sh, const unsigned char* kb, const u
 struct Geo {
     int G, cta, pos, nqkv, qd, kvd;
     int R, units, ug, ur;                // o_proj row slices per kv head; this CTA's unit (ug < 0: none)
+    int split, S, a0, a1;                // split attention: S units share the positions; this unit's [a0, a1)
     int q0, q1, o0, o1, c0, c1, m0, m1;  // tile ranges: qkv, o (unit rows), gate|up (8 channels), lm
 };
 
@@ -460,6 +463,13 @@ __device__ Geo make_geo(const B2MkPlan& p) {
     g.units = p.nkv * g.R;
     g.ug = g.cta < g.units ? g.cta / g.R : -1;
     g.ur = g.cta < g.units ? g.cta % g.R : 0;
+    // Up to 2 kKVPos cached positions every unit of a kv head attends over
+    // all of them; beyond, the first S units split them and publish partial
+    // softmax states that every unit of the head merges.
+    g.split = g.pos > 2 * kKVPos;
+    g.S = min(kSplit, g.R);
+    g.a0 = g.split ? (g.ur < g.S ? split_lo(g.pos, g.S, g.ur) : 0) : 0;
+    g.a1 = g.split ? (g.ur < g.S ? split_lo(g.pos, g.S, g.ur + 1) : 0) : g.pos;
     const int qt = g.nqkv / 16, ot = p.hidden / 16, ct = p.ffn / 8, mt = p.vocab / 16;
     g.q0 = split_lo(qt, g.G, g.cta);
     g.q1 = split_lo(qt, g.G, g.cta + 1);
@@ -579,14 +589,19 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
         if (geo.ug >= 0) {
             ctl(OP_AIN, l);
             const size_t head = (size_t)l * p.layer_stride + (size_t)geo.ug * p.max_seq * kHD;
-            for (int a = 0; a < geo.pos && !sh.pdead; a += kKVPos) {
-                const int b = min(geo.pos, a + kKVPos);
+            for (int a = geo.a0; a < geo.a1 && !sh.pdead; a += kKVPos) {
+                const int b = min(geo.a1, a + kKVPos);
                 const uint32_t by = (uint32_t)(b - a) * kHD * 2;
                 const void* src[2] = {p.k_cache + head + (size_t)a * kHD, p.v_cache + head + (size_t)a * kHD};
                 const uint32_t bys[2] = {by, by};
                 blocks(OP_KV, l, a, b, 2, src, bys);
             }
-            ctl(OP_AOUT, l);
+            if (geo.split) {
+                if (geo.ur < geo.S) ctl(OP_APUB, l);
+                ctl(OP_AMRG, l);
+            } else {
+                ctl(OP_AOUT, l);
+            }
             const int per = max(1, min(4, (int)(kOpMax / sub_o)));
             for (int a = geo.o0; a < geo.o1 && !sh.pdead; a += per) {
                 const int b = min(geo.o1, a + per);
@@ -827,6 +842,73 @@ struct Consumer {
         return vote(true);
     }
 
+    // Split attention, this unit's share: the warps' softmax states merged
+    // into one (max, sum, unnormalized output per q head) and published.
+    __device__ bool apub(int l) {
+        const int h = tid / kHD, d = tid % kHD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NC; w++) M = fmaxf(M, sh.mrg_m[w][h]);
+        float den = 0.f, num = 0.f;
+#pragma unroll
+        for (int w = 0; w < NC; w++) {
+            const float m = sh.mrg_m[w][h];
+            if (m == -INFINITY) continue;
+            const float c = expf(m - M);
+            den = fmaf(sh.mrg_l[w][h], c, den);
+            num = fmaf(sh.mrg_o[w][h][d], c, num);
+        }
+        unsigned long long* dst = S.apart + ((size_t)geo.ug * kSplit + geo.ur) * (4 + 2 * kHD);
+        const uint32_t t = ltag(l);
+        ll_put(dst + 4 + tid, num, t);
+        if (d == 0) {
+            ll_put(dst + 2 * h, M, t);
+            ll_put(dst + 2 * h + 1, den, t);
+        }
+        return true;
+    }
+
+    // Split attention, every unit of the head: warp w takes the published
+    // state of unit w (in unit order), then the merge of aout adds the newest
+    // position and normalizes.
+    __device__ bool amrg(int l) {
+        float4 o0 = make_float4(0.f, 0.f, 0.f, 0.f), o1 = o0;
+        float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+        bool ok = true;
+        if (warp < geo.S) {
+            const unsigned long long* src = S.apart + ((size_t)geo.ug * kSplit + warp) * (4 + 2 * kHD);
+            const uint32_t t = ltag(l);
+            for (long long it = 0;; it++) {
+                const ulonglong2 a = ll_get2(src), b = ll_get2(src + 2);
+                const ulonglong2 c = ll_get2(src + 4 + 4 * lane), e = ll_get2(src + 6 + 4 * lane);
+                const ulonglong2 f = ll_get2(src + 4 + kHD + 4 * lane), g = ll_get2(src + 6 + kHD + 4 * lane);
+                if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t) && ll_ok(c.x, t) &&
+                    ll_ok(c.y, t) && ll_ok(e.x, t) && ll_ok(e.y, t) && ll_ok(f.x, t) && ll_ok(f.y, t) &&
+                    ll_ok(g.x, t) && ll_ok(g.y, t)) {
+                    m0 = ll_val(a.x), l0 = ll_val(a.y), m1 = ll_val(b.x), l1 = ll_val(b.y);
+                    o0 = make_float4(ll_val(c.x), ll_val(c.y), ll_val(e.x), ll_val(e.y));
+                    o1 = make_float4(ll_val(f.x), ll_val(f.y), ll_val(g.x), ll_val(g.y));
+                    break;
+                }
+                if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                    if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                    ok = false;
+                    break;
+                }
+                if (it > 8) __nanosleep(32);
+            }
+        }
+        *reinterpret_cast<float4*>(&sh.mrg_o[warp][0][4 * lane]) = o0;
+        *reinterpret_cast<float4*>(&sh.mrg_o[warp][1][4 * lane]) = o1;
+        if (lane == 0) {
+            sh.mrg_m[warp][0] = m0, sh.mrg_l[warp][0] = l0;
+            sh.mrg_m[warp][1] = m1, sh.mrg_l[warp][1] = l1;
+        }
+        __syncwarp();
+        if (!vote(ok)) return false;
+        return aout();
+    }
+
     // The newest position (warp 0), then the merge of the warps' softmax
     // states into the FP16 attention output xo (the o_proj input).
     __device__ bool aout() {
@@ -1039,9 +1121,11 @@ struct Consumer {
         return ok;
     }
 
+    // Positions 8 w + 64 j of the operation (K rows, then V rows) in warp w.
     __device__ void kv_op(const Desc& d, const unsigned char* buf) {
-        const int n = d.b - d.a, i0 = warp * 8;
-        if (i0 < n) attend8(sh, buf + (size_t)i0 * 256, buf + (size_t)n * 256 + (size_t)i0 * 256, min(8, n - i0), warp, lane);
+        const int n = d.b - d.a;
+        for (int i0 = warp * 8; i0 < n; i0 += 8 * NC)
+            attend8(sh, buf + (size_t)i0 * 256, buf + (size_t)n * 256 + (size_t)i0 * 256, min(8, n - i0), warp, lane);
     }
 
     __device__ bool o_tiles(const Desc& d, const unsigned char* buf, int pb) {
@@ -1143,6 +1227,8 @@ struct Consumer {
                 case OP_AIN: ok = vote(true) && ain(d.l, d.c, d.d); break;
                 case OP_KV: kv_op(d, buf); break;
                 case OP_AOUT: ok = vote(true) && aout(); break;
+                case OP_APUB: ok = vote(true) && apub(d.l); break;
+                case OP_AMRG: ok = vote(true) && amrg(d.l); break;  // (apub's reads of the warp states are done)
                 case OP_O: ok = o_tiles(d, buf, pb ^= 1); break;
                 case OP_RO: ok = vote(true) && ro(d.l); break;
                 case OP_GIN: ok = gin(d.l); break;
@@ -1302,7 +1388,7 @@ int launch(const B2MkPlan* p, cudaStream_t s) {
 
 }  // namespace
 
-extern "C" int b2_mk2_max_context(void) { return kFuseMax; }
+extern "C" int b2_mk2_max_context(void) { return 1 << 30; }  // any context: long ones split over units
 
 extern "C" size_t b2_mk2_scratch_bytes(int n_layers, int hidden, int ffn, int nq, int nkv, int hd) {
     (void)ffn;

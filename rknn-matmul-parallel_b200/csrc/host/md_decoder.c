@@ -871,7 +871,14 @@ int matmul_decoder_prefill_batch(MatmulDecoderContext* ctx, const float* embeddi
 
 /* ─── state queries ─── */
 
-int matmul_decoder_uses_persistent_kernel(const MatmulDecoderContext* ctx) { return ctx && ctx->use_mk ? 1 : 0; }
+int matmul_decoder_uses_persistent_kernel(const MatmulDecoderContext* ctx) {
+    return ctx && (ctx->use_mk || ctx->use_mk2) ? 1 : 0;
+}
+
+int matmul_decoder_step_kernel(const MatmulDecoderContext* ctx, int n_cached) {
+    if (!ctx || n_cached < 0) return MATMUL_DECODER_ERR_INVALID_ARG;
+    return mk_kind(ctx, n_cached, 1);
+}
 
 void matmul_decoder_clear_kv_cache(MatmulDecoderContext* ctx) {
     if (ctx) ctx->seq_len = 0;

@@ -110,6 +110,7 @@ SIGNATURES = {
     "matmul_decoder_set_seq_len": (c_int, [c_vp, c_int]),
     "matmul_decoder_get_hidden": (c_int, [c_vp, c_vp]),
     "matmul_decoder_uses_persistent_kernel": (c_int, [c_vp]),
+    "matmul_decoder_step_kernel": (c_int, [c_vp, c_int]),
     "matmul_decoder_quantize_weight": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_quantize_lm_head": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_batch_create": (c_vp, [ctypes.c_char_p, c_vp, c_int, c_int, c_int]),
@@ -365,6 +366,10 @@ class Decoder:
 
     def uses_persistent_kernel(self):
         return bool(capi().matmul_decoder_uses_persistent_kernel(self.ctx))
+
+    def step_kernel(self, n_cached):
+        """2: tile-stream persistent kernel, 1: first persistent kernel, 0: graph."""
+        return capi().matmul_decoder_step_kernel(self.ctx, n_cached)
 
     def stats(self):
         s = MatmulDecoderStats()
