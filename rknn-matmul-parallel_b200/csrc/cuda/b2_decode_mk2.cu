@@ -68,7 +68,7 @@ constexpr int kND = 64;                // operation slots
 constexpr int kOpMax = 64 * 1024;      // bytes of one data operation
 constexpr int kOpRows = 64;            // rows (4 tiles) of one dot operation
 constexpr int kKVPos = 128;            // cached positions per K/V operation (K and V: 64 KB)
-constexpr int kSplit = 8;              // units of a kv head that share its positions above 2 kKVPos
+constexpr int kSplit = 2 * NC;         // units of a kv head that share its positions above 2 kKVPos
 constexpr int kMaxH = 4 * kCons;       // hidden: one float4 per consumer thread
 constexpr int kMaxF = 3072;            // longest staged activation
 constexpr int kMaxCh = 32;             // gate|up channels per CTA
@@ -868,36 +868,55 @@ struct Consumer {
         return true;
     }
 
-    // Split attention, every unit of the head: warp w takes the published
-    // state of unit w (in unit order), then the merge of aout adds the newest
-    // position and normalizes.
+    // One unit's published state (both q heads; this lane's 4 dims), polled
+    // until every word carries the tag.
+    __device__ bool poll_state(const unsigned long long* src, uint32_t t, float (&m)[kGq], float (&lv)[kGq],
+                               float4 (&o)[kGq]) const {
+        for (long long it = 0;; it++) {
+            const ulonglong2 a = ll_get2(src), b = ll_get2(src + 2);
+            const ulonglong2 c = ll_get2(src + 4 + 4 * lane), e = ll_get2(src + 6 + 4 * lane);
+            const ulonglong2 f = ll_get2(src + 4 + kHD + 4 * lane), g = ll_get2(src + 6 + kHD + 4 * lane);
+            if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t) && ll_ok(c.x, t) && ll_ok(c.y, t) &&
+                ll_ok(e.x, t) && ll_ok(e.y, t) && ll_ok(f.x, t) && ll_ok(f.y, t) && ll_ok(g.x, t) && ll_ok(g.y, t)) {
+                m[0] = ll_val(a.x), lv[0] = ll_val(a.y), m[1] = ll_val(b.x), lv[1] = ll_val(b.y);
+                o[0] = make_float4(ll_val(c.x), ll_val(c.y), ll_val(e.x), ll_val(e.y));
+                o[1] = make_float4(ll_val(f.x), ll_val(f.y), ll_val(g.x), ll_val(g.y));
+                return true;
+            }
+            if (it > limit || ((it & 63) == 63 && abort_seen())) {
+                if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
+                return false;
+            }
+            if (it > 8) __nanosleep(32);
+        }
+    }
+
+    // Split attention, every unit of the head: warp w merges the published
+    // states of units w and w + 8 (in that order), then the merge of aout adds
+    // the newest position, combines the warps in warp order and normalizes.
     __device__ bool amrg(int l) {
-        float4 o0 = make_float4(0.f, 0.f, 0.f, 0.f), o1 = o0;
-        float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+        float4 o[kGq] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+        float m[kGq] = {-INFINITY, -INFINITY}, lv[kGq] = {0.f, 0.f};
         bool ok = true;
-        if (warp < geo.S) {
-            const unsigned long long* src = S.apart + ((size_t)geo.ug * kSplit + warp) * (4 + 2 * kHD);
-            const uint32_t t = ltag(l);
-            for (long long it = 0;; it++) {
-                const ulonglong2 a = ll_get2(src), b = ll_get2(src + 2);
-                const ulonglong2 c = ll_get2(src + 4 + 4 * lane), e = ll_get2(src + 6 + 4 * lane);
-                const ulonglong2 f = ll_get2(src + 4 + kHD + 4 * lane), g = ll_get2(src + 6 + kHD + 4 * lane);
-                if (ll_ok(a.x, t) && ll_ok(a.y, t) && ll_ok(b.x, t) && ll_ok(b.y, t) && ll_ok(c.x, t) &&
-                    ll_ok(c.y, t) && ll_ok(e.x, t) && ll_ok(e.y, t) && ll_ok(f.x, t) && ll_ok(f.y, t) &&
-                    ll_ok(g.x, t) && ll_ok(g.y, t)) {
-                    m0 = ll_val(a.x), l0 = ll_val(a.y), m1 = ll_val(b.x), l1 = ll_val(b.y);
-                    o0 = make_float4(ll_val(c.x), ll_val(c.y), ll_val(e.x), ll_val(e.y));
-                    o1 = make_float4(ll_val(f.x), ll_val(f.y), ll_val(g.x), ll_val(g.y));
-                    break;
-                }
-                if (it > limit || ((it & 63) == 63 && abort_seen())) {
-                    if (it > limit) atomicOr(p.state + B2_MK_ERR, 1);
-                    ok = false;
-                    break;
-                }
-                if (it > 8) __nanosleep(32);
+        const uint32_t t = ltag(l);
+        for (int u = warp; u < geo.S && ok; u += NC) {
+            float mu[kGq], lu[kGq];
+            float4 ou[kGq];
+            ok = poll_state(S.apart + ((size_t)geo.ug * kSplit + u) * (4 + 2 * kHD), t, mu, lu, ou);
+            if (!ok) break;
+#pragma unroll
+            for (int h = 0; h < kGq; h++) {
+                if (mu[h] == -INFINITY) continue;
+                const float M = fmaxf(m[h], mu[h]);
+                const float c1 = m[h] == -INFINITY ? 0.f : expf(m[h] - M), c2 = expf(mu[h] - M);
+                lv[h] = lv[h] * c1 + lu[h] * c2;
+                o[h] = make_float4(o[h].x * c1 + ou[h].x * c2, o[h].y * c1 + ou[h].y * c2, o[h].z * c1 + ou[h].z * c2,
+                                   o[h].w * c1 + ou[h].w * c2);
+                m[h] = M;
             }
         }
+        const float4 o0 = o[0], o1 = o[1];
+        const float m0 = m[0], l0 = lv[0], m1 = m[1], l1 = lv[1];
         *reinterpret_cast<float4*>(&sh.mrg_o[warp][0][4 * lane]) = o0;
         *reinterpret_cast<float4*>(&sh.mrg_o[warp][1][4 * lane]) = o1;
         if (lane == 0) {
