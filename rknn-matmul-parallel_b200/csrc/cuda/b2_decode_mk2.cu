@@ -77,6 +77,7 @@ constexpr int kMaxG = 256;             // CTAs the partial arrays have room for
 constexpr int kMaxLayers = 32;         // layers of the shared-memory pointer table
 constexpr long long kDefaultPolls = 1ll << 22;
 static_assert(kCons == kGq * kHD, "the attention merge gives one consumer thread per (q head, dim)");
+static_assert(kKVPos == 16 * NC, "a K/V operation gives each warp 16 positions");
 
 enum Op : int {
     OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_APUB, OP_AMRG, OP_O, OP_RO, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND, OP_RD,
@@ -351,14 +352,16 @@ __device__ __forceinline__ int stage_pos(int e) {
     return e;
 }
 
-// Online softmax over up to 8 positions of one warp (K and V rows of 256
+// Online softmax over up to 16 positions of one warp (K and V rows of 256
 // bytes; lane owns dims 4 lane .. 4 lane + 3 of both q heads).  The warp's
 // softmax state (running max, sum and output per head) lives in
-// sh.mrg_m / mrg_l / mrg_o.  Scores of the 8 positions x 2 heads are reduced
-// across the warp in a transposed butterfly: afterwards lane l holds the
-// score with index (l >> 1) & 15 = 2 i + h.
-__device__ __forceinline__ void attend8(Sh& sh, const unsigned char* kb, const unsigned char* vb, int n, int warp,
-                                     int lane) {
+// sh.mrg_m / mrg_l / mrg_o.  The 32 partial scores (16 positions x 2 heads)
+// are reduced across the warp in a transposed butterfly: afterwards lane l
+// holds the score of position l >> 1, head l & 1.  Every loop has a
+// compile-time trip count (positions past n are predicated off), so the
+// chains unroll.
+__device__ __forceinline__ void attend16(Sh& sh, const unsigned char* kb, const unsigned char* vb, int n, int warp,
+                                         int lane) {
     const float scale = 0.08838834764831845f;  // 1/sqrt(128)
     float qv[kGq][4], ao[kGq][4], am[kGq], al[kGq];
 #pragma unroll
@@ -370,9 +373,9 @@ __device__ __forceinline__ void attend8(Sh& sh, const unsigned char* kb, const u
         am[h] = sh.mrg_m[warp][h];
         al[h] = sh.mrg_l[warp][h];
     }
-    float v[16];
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < 16; i++) {
         float2 k01 = make_float2(0.f, 0.f), k23 = k01;
         if (i < n) {
             const uint2 kk = *reinterpret_cast<const uint2*>(kb + i * 256 + lane * 8);
@@ -383,54 +386,58 @@ __device__ __forceinline__ void attend8(Sh& sh, const unsigned char* kb, const u
         for (int h = 0; h < kGq; h++)
             v[2 * i + h] = fmaf(qv[h][0], k01.x, fmaf(qv[h][1], k01.y, fmaf(qv[h][2], k23.x, qv[h][3] * k23.y)));
     }
-    // transposed butterfly: 16 sums in 16 shuffles
+    // transposed butterfly: 32 sums in 31 shuffles; lane l ends with value l
 #pragma unroll
-    for (int step = 0; step < 4; step++) {
-        const int half = 8 >> step;   // values kept after this step
+    for (int step = 0; step < 5; step++) {
+        const int half = 16 >> step;  // values kept after this step
         const int bit = 16 >> step;   // lane bit that selects the half
         const bool hi = (lane & bit) != 0;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 16; j++) {
             if (j >= half) break;
             const float send = hi ? v[j] : v[j + half];
             const float recv = __shfl_xor_sync(0xffffffffu, send, bit);
             v[j] = (hi ? v[j + half] : v[j]) + recv;
         }
     }
-    float s = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
-    const int idx = (lane >> 1) & 15, i = idx >> 1, h = idx & 1;
-    s = i < n ? s * scale : -INFINITY;
-    // per-head max and sum over the lanes holding that head (lane bits 2..4)
+    const int i = lane >> 1, h = lane & 1;
+    const float s = i < n ? v[0] * scale : -INFINITY;
+    // per-head max and sum over the lanes holding that head (lane bits 1..4)
     float mc = s;
+    mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 2));
     mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 4));
     mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 8));
     mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 16));
-    const float mo = __shfl_xor_sync(0xffffffffu, mc, 2);  // the other head's chunk max
+    const float mo = __shfl_xor_sync(0xffffffffu, mc, 1);  // the other head's chunk max
     const float mch0 = h == 0 ? mc : mo, mch1 = h == 0 ? mo : mc;
     const float mn0 = fmaxf(am[0], mch0), mn1 = fmaxf(am[1], mch1);
     const float c0 = am[0] == -INFINITY ? 0.f : expf(am[0] - mn0);
     const float c1 = am[1] == -INFINITY ? 0.f : expf(am[1] - mn1);
     const float pr = i < n ? expf(s - (h == 0 ? mn0 : mn1)) : 0.f;
     float ps = pr;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
     ps += __shfl_xor_sync(0xffffffffu, ps, 4);
     ps += __shfl_xor_sync(0xffffffffu, ps, 8);
     ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-    const float po = __shfl_xor_sync(0xffffffffu, ps, 2);
+    const float po = __shfl_xor_sync(0xffffffffu, ps, 1);
     al[0] = al[0] * c0 + (h == 0 ? ps : po);
     al[1] = al[1] * c1 + (h == 0 ? po : ps);
     am[0] = mn0;
     am[1] = mn1;
 #pragma unroll
     for (int j = 0; j < 4; j++) ao[0][j] *= c0, ao[1][j] *= c1;
-    for (int ii = 0; ii < n; ii++) {  // n is warp-uniform
-        const float p0 = __shfl_sync(0xffffffffu, pr, (2 * ii) << 1);
-        const float p1 = __shfl_sync(0xffffffffu, pr, (2 * ii + 1) << 1);
-        const uint2 vv = *reinterpret_cast<const uint2*>(vb + ii * 256 + lane * 8);
-        const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
-        ao[0][0] = fmaf(p0, v01.x, ao[0][0]), ao[0][1] = fmaf(p0, v01.y, ao[0][1]);
-        ao[0][2] = fmaf(p0, v23.x, ao[0][2]), ao[0][3] = fmaf(p0, v23.y, ao[0][3]);
-        ao[1][0] = fmaf(p1, v01.x, ao[1][0]), ao[1][1] = fmaf(p1, v01.y, ao[1][1]);
-        ao[1][2] = fmaf(p1, v23.x, ao[1][2]), ao[1][3] = fmaf(p1, v23.y, ao[1][3]);
+#pragma unroll
+    for (int ii = 0; ii < 16; ii++) {
+        const float p0 = __shfl_sync(0xffffffffu, pr, 2 * ii);
+        const float p1 = __shfl_sync(0xffffffffu, pr, 2 * ii + 1);
+        if (ii < n) {  // (warp-uniform)
+            const uint2 vv = *reinterpret_cast<const uint2*>(vb + ii * 256 + lane * 8);
+            const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
+            ao[0][0] = fmaf(p0, v01.x, ao[0][0]), ao[0][1] = fmaf(p0, v01.y, ao[0][1]);
+            ao[0][2] = fmaf(p0, v23.x, ao[0][2]), ao[0][3] = fmaf(p0, v23.y, ao[0][3]);
+            ao[1][0] = fmaf(p1, v01.x, ao[1][0]), ao[1][1] = fmaf(p1, v01.y, ao[1][1]);
+            ao[1][2] = fmaf(p1, v23.x, ao[1][2]), ao[1][3] = fmaf(p1, v23.y, ao[1][3]);
+        }
     }
 #pragma unroll
     for (int hh = 0; hh < kGq; hh++)
@@ -932,7 +939,7 @@ struct Consumer {
     // states into the FP16 attention output xo (the o_proj input).
     __device__ bool aout() {
         if (warp == 0)
-            attend8(sh, reinterpret_cast<const unsigned char*>(sh.knew), reinterpret_cast<const unsigned char*>(sh.vnew),
+            attend16(sh, reinterpret_cast<const unsigned char*>(sh.knew), reinterpret_cast<const unsigned char*>(sh.vnew),
                     1, warp, lane);
         if (!vote(true)) return false;
         {
@@ -1140,11 +1147,11 @@ struct Consumer {
         return ok;
     }
 
-    // Positions 8 w + 64 j of the operation (K rows, then V rows) in warp w.
+    // Positions 16 w .. 16 w + 15 of the operation (K rows, then V rows) in warp w.
     __device__ void kv_op(const Desc& d, const unsigned char* buf) {
-        const int n = d.b - d.a;
-        for (int i0 = warp * 8; i0 < n; i0 += 8 * NC)
-            attend8(sh, buf + (size_t)i0 * 256, buf + (size_t)n * 256 + (size_t)i0 * 256, min(8, n - i0), warp, lane);
+        const int n = d.b - d.a, i0 = warp * 16;
+        if (i0 < n)
+            attend16(sh, buf + (size_t)i0 * 256, buf + (size_t)n * 256 + (size_t)i0 * 256, min(16, n - i0), warp, lane);
     }
 
     __device__ bool o_tiles(const Desc& d, const unsigned char* buf, int pb) {
