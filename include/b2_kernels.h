@@ -278,6 +278,19 @@ int b2_sample_token(const float* logits, int V, const int* repeat_tokens, int n_
                     int top_k, float top_p, float temperature, unsigned long long seed, unsigned long long counter,
                     int* token, int* info, b2_stream_t s);
 
+/* ASR front end (examples/qwen3_asr/mel.py:6-67): the (128, T = n / 160)
+ * log-mel spectrogram of a 16 kHz FP32 waveform audio[n] (n > 200), reflect
+ * padding, periodic Hann window, 400-point DFT power, mel = filters^T . power
+ * with filters [201][128], log10 clamped at its maximum - 8, (x + 4) / 4.
+ * out is device FP32 [128][T]; work holds b2_log_mel_workspace(n) bytes. */
+size_t b2_log_mel_workspace(int n_samples);
+int b2_log_mel(const float* audio, int n_samples, const float* filters, float* out, void* work, b2_stream_t s);
+/* Decoder input rows (examples/qwen3_asr/engine.py:255-314): out[total][H] =
+ * table rows of prefix_ids, then the audio rows, then table rows of
+ * suffix_ids (all device pointers; ids must lie in [0, V)). */
+int b2_build_embed(const float* table, int V, int H, const int* prefix_ids, int n_pre, const float* audio,
+                   int n_audio, const int* suffix_ids, int n_suf, float* out, b2_stream_t s);
+
 /* Device-side greedy loop bookkeeping, run once per step after the argmax:
  * hist[loop[2]] = loop[0] (the token just produced, which is also the next
  * step's input), then loop[1] (position) and loop[2] (step counter) advance.

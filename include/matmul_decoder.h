@@ -313,6 +313,20 @@ int matmul_decoder_step_sample(MatmulDecoderContext* ctx, int token_id, const fl
                                const SamplingParams* params);
 int matmul_decoder_set_seed(MatmulDecoderContext* ctx, unsigned long long seed);
 
+/* ADDITIVE.  ASR front end on the GPU (the reference does it in numpy,
+ * examples/qwen3_asr/mel.py:52-67 and engine.py:255-314).
+ * matmul_log_mel: host FP32 waveform audio[n_samples] at 16 kHz (n_samples
+ * > 200) and mel filters [201][128] -> host mel_out [128][n_samples / 160],
+ * the Whisper-style log-mel features (returns the frame count or an error).
+ * matmul_decoder_build_embed: host token ids and host audio embeddings
+ * [n_audio][hidden_dim] -> host embed_out [n_pre + n_audio + n_suf][hidden],
+ * token rows taken from the context's embedding table on the device
+ * (returns the row count or an error; ids outside [0, vocab) are rejected). */
+int matmul_log_mel(const float* audio, int n_samples, const float* filters, float* mel_out);
+int matmul_decoder_build_embed(MatmulDecoderContext* ctx, const int* prefix_ids, int n_pre,
+                               const float* audio_embd, int n_audio, const int* suffix_ids, int n_suf,
+                               float* embed_out);
+
 /* ADDITIVE.  Greedy decode of n_tokens tokens with the token feedback kept on
  * the device: step i consumes the token produced by step i-1 (step 0 consumes
  * first_token), so the host neither copies a token nor synchronizes between

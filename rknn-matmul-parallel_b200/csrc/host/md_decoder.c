@@ -912,6 +912,40 @@ int matmul_decoder_get_hidden(MatmulDecoderContext* ctx, float* hidden_out) {
     return rc ? fail("get_hidden", rc) : MATMUL_DECODER_OK;
 }
 
+int matmul_decoder_build_embed(MatmulDecoderContext* ctx, const int* prefix_ids, int n_pre,
+                               const float* audio_embd, int n_audio, const int* suffix_ids, int n_suf,
+                               float* embed_out) {
+    if (!ctx || !embed_out || n_pre < 0 || n_audio < 0 || n_suf < 0 || (n_pre && !prefix_ids) ||
+        (n_audio && !audio_embd) || (n_suf && !suffix_ids))
+        return MATMUL_DECODER_ERR_INVALID_ARG;
+    const int V = ctx->model.cfg.vocab_size, H = ctx->model.cfg.hidden_dim;
+    for (int i = 0; i < n_pre; i++)
+        if (prefix_ids[i] < 0 || prefix_ids[i] >= V) return MATMUL_DECODER_ERR_INVALID_ARG;
+    for (int i = 0; i < n_suf; i++)
+        if (suffix_ids[i] < 0 || suffix_ids[i] >= V) return MATMUL_DECODER_ERR_INVALID_ARG;
+    const int total = n_pre + n_audio + n_suf;
+    if (total == 0) return 0;
+    b2_set_device(ctx->device);
+    const size_t ids_bytes = (((size_t)n_pre + n_suf) * 4 + 255) & ~(size_t)255;
+    const size_t a_bytes = ((size_t)n_audio * H * 4 + 255) & ~(size_t)255;
+    unsigned char* buf = NULL;
+    int rc = b2_malloc((void**)&buf, ids_bytes + a_bytes + (size_t)total * H * 4);
+    if (rc) return MATMUL_DECODER_ERR_MEMORY;
+    int* d_ids = (int*)buf;
+    float* d_audio = (float*)(buf + ids_bytes);
+    float* d_out = (float*)(buf + ids_bytes + a_bytes);
+    b2_stream_t s = ctx->stream;
+    if (!rc && n_pre) rc = b2_memcpy_h2d(d_ids, prefix_ids, (size_t)n_pre * 4, s);
+    if (!rc && n_suf) rc = b2_memcpy_h2d(d_ids + n_pre, suffix_ids, (size_t)n_suf * 4, s);
+    if (!rc && n_audio) rc = b2_memcpy_h2d(d_audio, audio_embd, (size_t)n_audio * H * 4, s);
+    if (!rc)
+        rc = b2_build_embed(ctx->model.emb, V, H, d_ids, n_pre, d_audio, n_audio, d_ids + n_pre, n_suf, d_out, s);
+    if (!rc) rc = b2_memcpy_d2h(embed_out, d_out, (size_t)total * H * 4, s);
+    if (!rc) rc = b2_stream_sync(s);
+    b2_free(buf);
+    return rc ? fail("build_embed", rc) : total;
+}
+
 /* Host [len][nkv][hd] <-> device [nkv][max_seq][hd] for one layer. */
 static int kv_transfer(MatmulDecoderContext* ctx, int layer, int start, int len, uint16_t* kh, uint16_t* vh,
                        int to_device) {

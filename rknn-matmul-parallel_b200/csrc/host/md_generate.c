@@ -167,3 +167,33 @@ void matmul_kv_cache_destroy(MatmulKVCache* cache) {
     free(cache->v_cache);
     free(cache);
 }
+
+/* ─── ASR front end (ADDITIVE) ───
+ * The log-mel features on the current device: the waveform and the filters
+ * go up, the (128, T) features come back. */
+int matmul_log_mel(const float* audio, int n_samples, const float* filters, float* mel_out) {
+    if (!audio || !filters || !mel_out || n_samples <= 200) return MATMUL_DECODER_ERR_INVALID_ARG;
+    const int T = n_samples / 160;
+    const size_t wbytes = b2_log_mel_workspace(n_samples);
+    const size_t a_bytes = ((size_t)n_samples * 4 + 255) & ~(size_t)255;
+    const size_t f_bytes = ((size_t)201 * 128 * 4 + 255) & ~(size_t)255;
+    const size_t o_bytes = ((size_t)T * 128 * 4 + 255) & ~(size_t)255;
+    unsigned char* buf = NULL;
+    int rc = b2_malloc((void**)&buf, a_bytes + f_bytes + o_bytes + wbytes);
+    if (rc) return MATMUL_DECODER_ERR_MEMORY;
+    float* d_audio = (float*)buf;
+    float* d_filters = (float*)(buf + a_bytes);
+    float* d_out = (float*)(buf + a_bytes + f_bytes);
+    void* d_work = buf + a_bytes + f_bytes + o_bytes;
+    if (!rc) rc = b2_memcpy_h2d(d_audio, audio, (size_t)n_samples * 4, NULL);
+    if (!rc) rc = b2_memcpy_h2d(d_filters, filters, (size_t)201 * 128 * 4, NULL);
+    if (!rc) rc = b2_log_mel(d_audio, n_samples, d_filters, d_out, d_work, NULL);
+    if (!rc && T > 0) rc = b2_memcpy_d2h(mel_out, d_out, (size_t)T * 128 * 4, NULL);
+    if (!rc) rc = b2_stream_sync(NULL);
+    b2_free(buf);
+    if (rc) {
+        MD_LOG("log-mel failed (%d): %s\n", rc, b2_last_error());
+        return rc;
+    }
+    return T;
+}

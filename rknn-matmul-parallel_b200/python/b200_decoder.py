@@ -105,6 +105,8 @@ SIGNATURES = {
     "matmul_decoder_decode_greedy": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_step_sample": (c_int, [c_vp, c_int, c_vp, c_vp]),
     "matmul_decoder_set_seed": (c_int, [c_vp, ctypes.c_ulonglong]),
+    "matmul_log_mel": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "matmul_decoder_build_embed": (c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp]),
     "matmul_decoder_set_kv": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_get_kv": (c_int, [c_vp, c_int, c_int, c_int, c_vp, c_vp]),
     "matmul_decoder_set_seq_len": (c_int, [c_vp, c_int]),
@@ -125,6 +127,9 @@ SIGNATURES = {
     # b2_kernels.h
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_sample_max_vocab": (c_size, []),
+    "b2_log_mel_workspace": (c_size, [c_int]),
+    "b2_log_mel": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "b2_build_embed": (c_int, [c_vp, c_int, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     "b2_sample_token": (c_int, [c_vp, c_int, c_vp, c_int, ctypes.c_float, c_int, ctypes.c_float, ctypes.c_float,
                                 ctypes.c_ulonglong, ctypes.c_ulonglong, c_vp, c_vp, c_vp]),
     "b2_device_count": (c_int, [c_vp]),
