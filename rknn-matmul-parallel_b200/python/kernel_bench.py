@@ -5,13 +5,16 @@ workloads (Qwen3-0.6B: hidden 1024, 16 q / 8 kv heads of 128, ffn 3072).
     python rknn-matmul-parallel_b200/python/kernel_bench.py attn-split  [--rows 64]
     python rknn-matmul-parallel_b200/python/kernel_bench.py gemm-gu     [--rows 64] [--wtype i4] [--split 0]
     (gemm-qkv, gemm-o, gemm-down likewise)
+    python rknn-matmul-parallel_b200/python/kernel_bench.py log-mel     [--seconds 30]
 
 Attention rows are independent sequences whose cache lengths are drawn
 uniformly from [128, 4096) (the batched-decode workload, seeded); GEMM
 weights are random bytes of the given type.  Each timed iteration follows
 a 256 MB write that flushes L2; the line printed per case gives the median
 and minimum device time (CUDA events around the C-ABI call) and the
-algorithmic bytes (weights, or the K and V rows attended) per microsecond.
+algorithmic bytes (weights, or the K and V rows attended) per microsecond;
+for log-mel (the ASR front end) the FLOPs of the direct 400-point DFT and
+the mel product per second.
 Every kernel runs through the library's C-ABI (libmatmul_decoder.so)."""
 from __future__ import annotations
 
@@ -38,7 +41,8 @@ WTYPES = {"f16": (bd.W_F16, 2.0), "i8": (bd.W_I8, 1.0), "i4": (bd.W_I4, 0.5)}
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("kernel", choices=["attn-blocks", "attn-split"] + sorted(GEMMS))
+    ap.add_argument("kernel", choices=["attn-blocks", "attn-split", "log-mel"] + sorted(GEMMS))
+    ap.add_argument("--seconds", type=float, default=30.0, help="log-mel: audio length at 16 kHz")
     ap.add_argument("--rows", type=int, default=64, help="token rows (sequences for attention)")
     ap.add_argument("--wtype", choices=sorted(WTYPES), default="i4")
     ap.add_argument("--split", type=int, default=0, help="GEMM split-K cluster size (0: automatic)")
@@ -58,7 +62,21 @@ def main() -> int:
     M = a.rows
     keep = []
 
-    if a.kernel in GEMMS:
+    if a.kernel == "log-mel":
+        n = int(a.seconds * 16000)
+        audio = torch.from_numpy((0.1 * rng.standard_normal(n)).astype(np.float32)).to(dev)
+        filt = torch.from_numpy(rng.random((201, 128), dtype=np.float32) * 0.01).to(dev)
+        out = torch.empty((128, n // 160), dtype=torch.float32, device=dev)
+        work = torch.empty(lib.b2_log_mel_workspace(n), dtype=torch.uint8, device=dev)
+        keep += [audio, filt, out, work]
+        frames = n // 160 + 1
+        nbytes = frames * 201 * 400 * 4.0 + frames * 128 * 201 * 2.0  # FLOPs here
+        label = f"log-mel {a.seconds:g} s audio ({frames} frames)"
+
+        def run():
+            bd.check(lib.b2_log_mel(audio.data_ptr(), n, filt.data_ptr(), out.data_ptr(), work.data_ptr(), stream),
+                     a.kernel)
+    elif a.kernel in GEMMS:
         epi, K, N = GEMMS[a.kernel]
         wt, bpw = WTYPES[a.wtype]
         rows = 2 * N if epi == bd.EPI_SILU_PAIR else N
@@ -120,7 +138,8 @@ def main() -> int:
         torch.cuda.synchronize()
         times.append(t0.elapsed_time(t1) * 1e3)
     med = sorted(times)[len(times) // 2]
-    print(f"{label}: median {med:.1f} us, min {min(times):.1f} us, {nbytes / med / 1e3:.1f} GB/s algorithmic")
+    unit = "GFLOP/s" if a.kernel == "log-mel" else "GB/s"
+    print(f"{label}: median {med:.1f} us, min {min(times):.1f} us, {nbytes / med / 1e3:.1f} {unit} algorithmic")
     return 0
 
 
