@@ -591,10 +591,12 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
     };
     for (int l = 0; l < p.n_layers && !sh.pdead; l++) {
         const B2MkLayer& Lw = p.layers[l];
-        ctl(OP_XIN, l);
+        if (geo.q0 == geo.q1) ctl(OP_XIN, l);  // else the first q|k|v operation stages x
         stream(OP_QKV, l, Lw.qkv_t, geo.q0, geo.q1, tb_h, kOpRows / 16);
         if (geo.ug >= 0) {
-            ctl(OP_AIN, l);
+            // the first K/V operation also runs AIN, the last one AOUT (or APUB)
+            const bool has_kv = geo.a0 < geo.a1;
+            if (!has_kv) ctl(OP_AIN, l);
             const size_t head = (size_t)l * p.layer_stride + (size_t)geo.ug * p.max_seq * kHD;
             for (int a = geo.a0; a < geo.a1 && !sh.pdead; a += kKVPos) {
                 const int b = min(geo.a1, a + kKVPos);
@@ -604,9 +606,9 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
                 blocks(OP_KV, l, a, b, 2, src, bys);
             }
             if (geo.split) {
-                if (geo.ur < geo.S) ctl(OP_APUB, l);
+                if (geo.ur < geo.S && !has_kv) ctl(OP_APUB, l);
                 ctl(OP_AMRG, l);
-            } else {
+            } else if (!has_kv) {
                 ctl(OP_AOUT, l);
             }
             const int per = max(1, min(4, (int)(kOpMax / sub_o)));
@@ -621,12 +623,12 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
                 blocks(OP_O, l, a, b, b - a, src, bys);
             }
         }
-        ctl(OP_RO, l);
-        ctl(OP_GIN, l);
+        ctl(OP_RO, l);  // RO, then GIN
         stream(OP_GU, l, Lw.gu_t, geo.c0, geo.c1, tb_h, kOpRows / 16);
-        ctl(OP_ACT, l);
-        stream(OP_DN, l, Lw.dn_t, 8 * geo.c0, 8 * geo.c1, rb_h, kMaxCh);  // input-major down rows of the CTA's channels
-        ctl(OP_DEND, l);
+        // input-major down rows of the CTA's channels (one operation: the act
+        // barrier first, DEND at its end); without channels a zero partial
+        if (geo.c0 == geo.c1) ctl(OP_DEND, l);
+        else stream(OP_DN, l, Lw.dn_t, 8 * geo.c0, 8 * geo.c1, rb_h, kMaxCh);
         ctl(OP_RD, l);
     }
     if (p.do_lm) {
@@ -837,7 +839,7 @@ struct Consumer {
                 if (cache) cache[e0 + j] = v;
             }
         }
-        // every warp's softmax state starts empty
+        // every softmax state starts empty
 #pragma unroll
         for (int hh = 0; hh < kGq; hh++) {
             *reinterpret_cast<float4*>(&sh.mrg_o[warp][hh][e0]) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -852,25 +854,18 @@ struct Consumer {
     // Split attention, this unit's share: the warps' softmax states merged
     // into one (max, sum, unnormalized output per q head) and published.
     __device__ bool apub(int l) {
-        const int h = tid / kHD, d = tid % kHD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NC; w++) M = fmaxf(M, sh.mrg_m[w][h]);
-        float den = 0.f, num = 0.f;
-#pragma unroll
-        for (int w = 0; w < NC; w++) {
-            const float m = sh.mrg_m[w][h];
-            if (m == -INFINITY) continue;
-            const float c = expf(m - M);
-            den = fmaf(sh.mrg_l[w][h], c, den);
-            num = fmaf(sh.mrg_o[w][h][d], c, num);
-        }
         unsigned long long* dst = S.apart + ((size_t)geo.ug * kSplit + geo.ur) * (4 + 2 * kHD);
         const uint32_t t = ltag(l);
-        ll_put(dst + 4 + tid, num, t);
-        if (d == 0) {
-            ll_put(dst + 2 * h, M, t);
-            ll_put(dst + 2 * h + 1, den, t);
+        // (called after a barrier that follows the last attend_op)
+        if ((lane >> 3) == 0) {
+            const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7);
+            const float4 uo = *reinterpret_cast<const float4*>(&sh.mrg_o[0][hv][4 * dq]);
+            unsigned long long* o = dst + 4 + hv * kHD + 4 * dq;
+            ll_put(o, uo.x, t), ll_put(o + 1, uo.y, t), ll_put(o + 2, uo.z, t), ll_put(o + 3, uo.w, t);
+        }
+        if (tid < kGq) {
+            ll_put(dst + 2 * tid, sh.mrg_m[0][tid], t);
+            ll_put(dst + 2 * tid + 1, sh.mrg_l[0][tid], t);
         }
         return true;
     }
@@ -932,12 +927,130 @@ struct Consumer {
         }
         __syncwarp();
         if (!vote(ok)) return false;
-        return aout();
+        return aout_merge();
+    }
+
+    // All consumer threads: online softmax over n <= kKVPos positions (K and V
+    // rows of 256 bytes) into the unit's state in slot 0 of sh.mrg_m / mrg_l /
+    // mrg_o.  Thread 0 writes the max and sum after the last barrier (every
+    // thread reads them after the next call's first barrier); each output
+    // element has one owner thread, which alone reads and writes it.
+    //  1. scores: thread t takes position t >> 1, q head t & 1, the 128-dim
+    //     dot product over 16-byte chunks in a per-position rotated order (the
+    //     rows sit 256 bytes apart, so unrotated chunks would share banks);
+    //  2. per-head maximum and exponentials (warp shuffles, then the eight
+    //     warps' values through shared memory);
+    //  3. P.V: thread (head warp >> 2, dims 4 dq .. + 3, quarter lane >> 3)
+    //     sums a quarter of the positions; the quarters meet by shuffles.
+    __device__ bool attend_op(const unsigned char* kb, const unsigned char* vb, int n) {
+        float* pr = reinterpret_cast<float*>(sh.xs[1]);  // [kGq][kKVPos] probabilities (free during attention)
+        float* wmax = pr + kGq * kKVPos;                  // [NC][kGq]
+        float* wsum = wmax + NC * kGq;                    // [NC][kGq]
+        const float scale = 0.08838834764831845f;         // 1/sqrt(128)
+        const int i = tid >> 1, h = tid & 1;
+        float sc = -INFINITY;
+        if (i < n) {
+            const unsigned char* kr = kb + (size_t)i * 256;
+            const float* q = sh.sq[h];
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 2
+            for (int c = 0; c < 16; c++) {
+                const int cc = (c + i) & 15;
+                const uint4 kk = *reinterpret_cast<const uint4*>(kr + cc * 16);
+                const float4 qa = *reinterpret_cast<const float4*>(q + cc * 8);
+                const float4 qb = *reinterpret_cast<const float4*>(q + cc * 8 + 4);
+                const float2 k0 = b2::h2_to_f2(kk.x), k1 = b2::h2_to_f2(kk.y);
+                const float2 k2 = b2::h2_to_f2(kk.z), k3 = b2::h2_to_f2(kk.w);
+                a0 = fmaf(qa.x, k0.x, fmaf(qa.y, k0.y, a0));
+                a1 = fmaf(qa.z, k1.x, fmaf(qa.w, k1.y, a1));
+                a2 = fmaf(qb.x, k2.x, fmaf(qb.y, k2.y, a2));
+                a3 = fmaf(qb.z, k3.x, fmaf(qb.w, k3.y, a3));
+            }
+            sc = ((a0 + a1) + (a2 + a3)) * scale;
+        }
+        float m = sc;
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (lane < kGq) wmax[warp * kGq + lane] = m;  // lane h holds head h
+        if (!vote(true)) return false;
+        float mn[kGq], c[kGq];
+#pragma unroll
+        for (int hh = 0; hh < kGq; hh++) {
+            const float mo = sh.mrg_m[0][hh];
+            float M = mo;
+#pragma unroll
+            for (int w = 0; w < NC; w++) M = fmaxf(M, wmax[w * kGq + hh]);
+            mn[hh] = M;
+            c[hh] = mo == -INFINITY ? 0.f : expf(mo - M);
+        }
+        const float pe = i < n ? expf(sc - (h == 0 ? mn[0] : mn[1])) : 0.f;
+        if (i < kKVPos) pr[h * kKVPos + i] = pe;
+        float ps = pe;
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+        if (lane < kGq) wsum[warp * kGq + lane] = ps;
+        if (!vote(true)) return false;
+        float lnew[kGq];
+#pragma unroll
+        for (int hh = 0; hh < kGq; hh++) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < NC; w++) t += wsum[w * kGq + hh];
+            lnew[hh] = sh.mrg_l[0][hh] * c[hh] + t;
+        }
+        const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7), pq = lane >> 3;
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        const float* ph = pr + hv * kKVPos + pq * (kKVPos / 4);
+        const unsigned char* vr = vb + (size_t)pq * (kKVPos / 4) * 256 + dq * 8;
+#pragma unroll 8
+        for (int j = 0; j < kKVPos / 4; j++) {
+            if (pq * (kKVPos / 4) + j >= n) break;
+            const float pj = ph[j];
+            const uint2 vv = *reinterpret_cast<const uint2*>(vr + (size_t)j * 256);
+            const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
+            o0 = fmaf(pj, v01.x, o0), o1 = fmaf(pj, v01.y, o1), o2 = fmaf(pj, v23.x, o2), o3 = fmaf(pj, v23.y, o3);
+        }
+        o0 += __shfl_xor_sync(0xffffffffu, o0, 8), o1 += __shfl_xor_sync(0xffffffffu, o1, 8);
+        o2 += __shfl_xor_sync(0xffffffffu, o2, 8), o3 += __shfl_xor_sync(0xffffffffu, o3, 8);
+        o0 += __shfl_xor_sync(0xffffffffu, o0, 16), o1 += __shfl_xor_sync(0xffffffffu, o1, 16);
+        o2 += __shfl_xor_sync(0xffffffffu, o2, 16), o3 += __shfl_xor_sync(0xffffffffu, o3, 16);
+        if (pq == 0) {
+            const float cv = hv == 0 ? c[0] : c[1];
+            float4* uo = reinterpret_cast<float4*>(&sh.mrg_o[0][hv][4 * dq]);
+            const float4 u = *uo;
+            *uo = make_float4(fmaf(u.x, cv, o0), fmaf(u.y, cv, o1), fmaf(u.z, cv, o2), fmaf(u.w, cv, o3));
+        }
+        if (!vote(true)) return false;  // the state and probabilities are read before they change
+        if (tid == 0) {
+#pragma unroll
+            for (int hh = 0; hh < kGq; hh++) sh.mrg_m[0][hh] = mn[hh], sh.mrg_l[0][hh] = lnew[hh];
+        }
+        return true;
+    }
+
+    // Non-split attention: the newest position, then xo = output / sum.
+    __device__ bool aout() {
+        if (!attend_op(reinterpret_cast<const unsigned char*>(sh.knew), reinterpret_cast<const unsigned char*>(sh.vnew), 1))
+            return false;
+        if (!vote(true)) return false;  // thread 0's sums are in
+        if ((lane >> 3) == 0) {
+            const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7);
+            const float inv = 1.0f / sh.mrg_l[0][hv];
+            const float4 uo = *reinterpret_cast<const float4*>(&sh.mrg_o[0][hv][4 * dq]);
+            const float v[4] = {uo.x, uo.y, uo.z, uo.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) sh.xo[stage_pos<WT>(hv * kHD + 4 * dq + j)] = __float2half_rn(v[j] * inv);
+        }
+        return vote(true);
     }
 
     // The newest position (warp 0), then the merge of the warps' softmax
     // states into the FP16 attention output xo (the o_proj input).
-    __device__ bool aout() {
+    __device__ bool aout_merge() {
         if (warp == 0)
             attend16(sh, reinterpret_cast<const unsigned char*>(sh.knew), reinterpret_cast<const unsigned char*>(sh.vnew),
                     1, warp, lane);
@@ -1147,11 +1260,10 @@ struct Consumer {
         return ok;
     }
 
-    // Positions 16 w .. 16 w + 15 of the operation (K rows, then V rows) in warp w.
-    __device__ void kv_op(const Desc& d, const unsigned char* buf) {
-        const int n = d.b - d.a, i0 = warp * 16;
-        if (i0 < n)
-            attend16(sh, buf + (size_t)i0 * 256, buf + (size_t)n * 256 + (size_t)i0 * 256, min(16, n - i0), warp, lane);
+    // The operation's positions: K rows, then V rows.
+    __device__ bool kv_op(const Desc& d, const unsigned char* buf) {
+        const int n = d.b - d.a;
+        return attend_op(buf, buf + (size_t)n * 256, n);
     }
 
     __device__ bool o_tiles(const Desc& d, const unsigned char* buf, int pb) {
@@ -1186,9 +1298,12 @@ struct Consumer {
         const int n = 4 * tid;
         if (n >= p.hidden) return;
         const int rb = row_bytes(WT, p.hidden), base = 8 * geo.c0;
-        for (int j = d.a; j < d.b; j++) {
+#pragma unroll 8
+        for (int jj = 0; jj < kMaxCh; jj++) {
+            const int j = d.a + jj;
+            if (j >= d.b) break;
             const float a = sh.act[j - base];
-            const unsigned char* row = buf + (size_t)(j - d.a) * rb;
+            const unsigned char* row = buf + (size_t)jj * rb;
             float w[4];
             if constexpr (WT == B2_W_F16) {
                 const uint2 h = *reinterpret_cast<const uint2*>(row + n * 2);
@@ -1249,18 +1364,29 @@ struct Consumer {
             bool ok = true;
             switch (d.op) {
                 case OP_XIN: ok = xin(d.l); break;
-                case OP_QKV: ok = qkv_tiles(d, buf, pb ^= 1); break;
+                case OP_QKV:
+                    pb ^= 1;
+                    ok = (d.a != geo.q0 || xin(d.l)) && qkv_tiles(d, buf, pb);
+                    break;
                 case OP_AIN: ok = vote(true) && ain(d.l, d.c, d.d); break;
-                case OP_KV: kv_op(d, buf); break;
+                case OP_KV:
+                    ok = d.a != geo.a0 || (vote(true) && ain(d.l, d.c, d.d));
+                    ok = ok && kv_op(d, buf);
+                    if (ok && d.b == geo.a1) ok = vote(true) && (geo.split ? apub(d.l) : aout());
+                    break;
                 case OP_AOUT: ok = vote(true) && aout(); break;
                 case OP_APUB: ok = vote(true) && apub(d.l); break;
                 case OP_AMRG: ok = vote(true) && amrg(d.l); break;  // (apub's reads of the warp states are done)
                 case OP_O: ok = o_tiles(d, buf, pb ^= 1); break;
-                case OP_RO: ok = vote(true) && ro(d.l); break;
+                case OP_RO: ok = vote(true) && ro(d.l) && gin(d.l); break;
                 case OP_GIN: ok = gin(d.l); break;
                 case OP_GU: ok = gu_tiles(d, buf, pb ^= 1); break;
                 case OP_ACT: ok = vote(true); break;
-                case OP_DN: dn_rows(d, buf); break;
+                case OP_DN:
+                    ok = d.a != 8 * geo.c0 || vote(true);  // every channel's act is in shared memory
+                    if (ok) dn_rows(d, buf);
+                    if (ok && d.b == 8 * geo.c1) ok = dend(d.l);
+                    break;
                 case OP_DEND: ok = vote(true) && dend(d.l); break;
                 case OP_RD: ok = vote(true) && rd(d.l); break;
                 case OP_LIN: ok = lin(); break;
