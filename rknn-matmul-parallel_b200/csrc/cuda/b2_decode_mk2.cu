@@ -68,7 +68,9 @@ constexpr int kND = 64;                // operation slots
 constexpr int kOpMax = 64 * 1024;      // bytes of one data operation
 constexpr int kOpRows = 64;            // rows (4 tiles) of one dot operation
 constexpr int kKVPos = 128;            // cached positions per K/V operation (K and V: 64 KB)
-constexpr int kSplit = 2 * NC;         // units of a kv head that share its positions above 2 kKVPos
+constexpr int kKVPosNew = 120;         // ... of an unsplit head, whose last operation adds the newest
+constexpr int kAttMax = 128;           // positions of one attention step
+constexpr int kSplit = 2 * NC;         // units of a kv head that share its positions above 2 kKVPosNew
 constexpr int kMaxH = 4 * kCons;       // hidden: one float4 per consumer thread
 constexpr int kMaxF = 3072;            // longest staged activation
 constexpr int kMaxCh = 32;             // gate|up channels per CTA
@@ -77,7 +79,8 @@ constexpr int kMaxG = 256;             // CTAs the partial arrays have room for
 constexpr int kMaxLayers = 32;         // layers of the shared-memory pointer table
 constexpr long long kDefaultPolls = 1ll << 22;
 static_assert(kCons == kGq * kHD, "the attention merge gives one consumer thread per (q head, dim)");
-static_assert(kKVPos == 16 * NC, "a K/V operation gives each warp 16 positions");
+static_assert(kKVPos <= kAttMax && kKVPosNew < kAttMax && kAttMax == kCons / kGq,
+              "an attention step gives each thread one (position, head)");
 
 enum Op : int {
     OP_XIN, OP_QKV, OP_AIN, OP_KV, OP_AOUT, OP_APUB, OP_AMRG, OP_O, OP_RO, OP_GIN, OP_GU, OP_ACT, OP_DN, OP_DEND, OP_RD,
@@ -470,10 +473,10 @@ __device__ Geo make_geo(const B2MkPlan& p) {
     g.units = p.nkv * g.R;
     g.ug = g.cta < g.units ? g.cta / g.R : -1;
     g.ur = g.cta < g.units ? g.cta % g.R : 0;
-    // Up to 2 kKVPos cached positions every unit of a kv head attends over
+    // Up to 2 kKVPosNew cached positions every unit of a kv head attends over
     // all of them; beyond, the first S units split them and publish partial
     // softmax states that every unit of the head merges.
-    g.split = g.pos > 2 * kKVPos;
+    g.split = g.pos > 2 * kKVPosNew;
     g.S = min(kSplit, g.R);
     g.a0 = g.split ? (g.ur < g.S ? split_lo(g.pos, g.S, g.ur) : 0) : 0;
     g.a1 = g.split ? (g.ur < g.S ? split_lo(g.pos, g.S, g.ur + 1) : 0) : g.pos;
@@ -598,8 +601,9 @@ __device__ void produce(const B2MkPlan& p, const Geo& geo, Sh& sh, unsigned char
             const bool has_kv = geo.a0 < geo.a1;
             if (!has_kv) ctl(OP_AIN, l);
             const size_t head = (size_t)l * p.layer_stride + (size_t)geo.ug * p.max_seq * kHD;
-            for (int a = geo.a0; a < geo.a1 && !sh.pdead; a += kKVPos) {
-                const int b = min(geo.a1, a + kKVPos);
+            const int per_kv = geo.split ? kKVPos : kKVPosNew;
+            for (int a = geo.a0; a < geo.a1 && !sh.pdead; a += per_kv) {
+                const int b = min(geo.a1, a + per_kv);
                 const uint32_t by = (uint32_t)(b - a) * kHD * 2;
                 const void* src[2] = {p.k_cache + head + (size_t)a * kHD, p.v_cache + head + (size_t)a * kHD};
                 const uint32_t bys[2] = {by, by};
@@ -930,8 +934,9 @@ struct Consumer {
         return aout_merge();
     }
 
-    // All consumer threads: online softmax over n <= kKVPos positions (K and V
-    // rows of 256 bytes) into the unit's state in slot 0 of sh.mrg_m / mrg_l /
+    // All consumer threads: online softmax over n <= kAttMax positions (K and V
+    // rows of 256 bytes), and the newest position (sh.knew / vnew) after them
+    // when with_new, into the unit's state in slot 0 of sh.mrg_m / mrg_l /
     // mrg_o.  Thread 0 writes the max and sum after the last barrier (every
     // thread reads them after the next call's first barrier); each output
     // element has one owner thread, which alone reads and writes it.
@@ -942,15 +947,15 @@ struct Consumer {
     //     warps' values through shared memory);
     //  3. P.V: thread (head warp >> 2, dims 4 dq .. + 3, quarter lane >> 3)
     //     sums a quarter of the positions; the quarters meet by shuffles.
-    __device__ bool attend_op(const unsigned char* kb, const unsigned char* vb, int n) {
-        float* pr = reinterpret_cast<float*>(sh.xs[1]);  // [kGq][kKVPos] probabilities (free during attention)
-        float* wmax = pr + kGq * kKVPos;                  // [NC][kGq]
+    __device__ bool attend_op(const unsigned char* kb, const unsigned char* vb, int n, bool with_new) {
+        float* pr = reinterpret_cast<float*>(sh.xs[1]);  // [kGq][kAttMax] probabilities (free during attention)
+        float* wmax = pr + kGq * kAttMax;                 // [NC][kGq]
         float* wsum = wmax + NC * kGq;                    // [NC][kGq]
         const float scale = 0.08838834764831845f;         // 1/sqrt(128)
-        const int i = tid >> 1, h = tid & 1;
+        const int i = tid >> 1, h = tid & 1, m_all = n + (with_new ? 1 : 0);
         float sc = -INFINITY;
-        if (i < n) {
-            const unsigned char* kr = kb + (size_t)i * 256;
+        if (i < m_all) {
+            const unsigned char* kr = i < n ? kb + (size_t)i * 256 : reinterpret_cast<const unsigned char*>(sh.knew);
             const float* q = sh.sq[h];
             float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll 2
@@ -985,8 +990,8 @@ struct Consumer {
             mn[hh] = M;
             c[hh] = mo == -INFINITY ? 0.f : expf(mo - M);
         }
-        const float pe = i < n ? expf(sc - (h == 0 ? mn[0] : mn[1])) : 0.f;
-        if (i < kKVPos) pr[h * kKVPos + i] = pe;
+        const float pe = i < m_all ? expf(sc - (h == 0 ? mn[0] : mn[1])) : 0.f;
+        pr[h * kAttMax + i] = pe;
         float ps = pe;
         ps += __shfl_xor_sync(0xffffffffu, ps, 2);
         ps += __shfl_xor_sync(0xffffffffu, ps, 4);
@@ -1004,13 +1009,14 @@ struct Consumer {
         }
         const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7), pq = lane >> 3;
         float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        const float* ph = pr + hv * kKVPos + pq * (kKVPos / 4);
-        const unsigned char* vr = vb + (size_t)pq * (kKVPos / 4) * 256 + dq * 8;
+        const float* ph = pr + hv * kAttMax + pq * (kAttMax / 4);
 #pragma unroll 8
-        for (int j = 0; j < kKVPos / 4; j++) {
-            if (pq * (kKVPos / 4) + j >= n) break;
+        for (int j = 0; j < kAttMax / 4; j++) {
+            const int ix = pq * (kAttMax / 4) + j;
+            if (ix >= m_all) break;
             const float pj = ph[j];
-            const uint2 vv = *reinterpret_cast<const uint2*>(vr + (size_t)j * 256);
+            const unsigned char* vr = ix < n ? vb + (size_t)ix * 256 : reinterpret_cast<const unsigned char*>(sh.vnew);
+            const uint2 vv = *reinterpret_cast<const uint2*>(vr + dq * 8);
             const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
             o0 = fmaf(pj, v01.x, o0), o1 = fmaf(pj, v01.y, o1), o2 = fmaf(pj, v23.x, o2), o3 = fmaf(pj, v23.y, o3);
         }
@@ -1032,10 +1038,11 @@ struct Consumer {
         return true;
     }
 
-    // Non-split attention: the newest position, then xo = output / sum.
-    __device__ bool aout() {
-        if (!attend_op(reinterpret_cast<const unsigned char*>(sh.knew), reinterpret_cast<const unsigned char*>(sh.vnew), 1))
-            return false;
+    // Non-split attention without cached positions: the newest position alone.
+    __device__ bool aout() { return attend_op(nullptr, nullptr, 0, true) && finish_out(); }
+
+    // xo = output / sum of the unit's state (after the last attention step).
+    __device__ bool finish_out() {
         if (!vote(true)) return false;  // thread 0's sums are in
         if ((lane >> 3) == 0) {
             const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7);
@@ -1260,10 +1267,11 @@ struct Consumer {
         return ok;
     }
 
-    // The operation's positions: K rows, then V rows.
-    __device__ bool kv_op(const Desc& d, const unsigned char* buf) {
+    // The operation's positions (K rows, then V rows), and the newest one
+    // after the last operation of an unsplit head.
+    __device__ bool kv_op(const Desc& d, const unsigned char* buf, bool with_new) {
         const int n = d.b - d.a;
-        return attend_op(buf, buf + (size_t)n * 256, n);
+        return attend_op(buf, buf + (size_t)n * 256, n, with_new);
     }
 
     __device__ bool o_tiles(const Desc& d, const unsigned char* buf, int pb) {
@@ -1371,8 +1379,8 @@ struct Consumer {
                 case OP_AIN: ok = vote(true) && ain(d.l, d.c, d.d); break;
                 case OP_KV:
                     ok = d.a != geo.a0 || (vote(true) && ain(d.l, d.c, d.d));
-                    ok = ok && kv_op(d, buf);
-                    if (ok && d.b == geo.a1) ok = vote(true) && (geo.split ? apub(d.l) : aout());
+                    ok = ok && kv_op(d, buf, d.b == geo.a1 && !geo.split);
+                    if (ok && d.b == geo.a1) ok = geo.split ? (vote(true) && apub(d.l)) : finish_out();
                     break;
                 case OP_AOUT: ok = vote(true) && aout(); break;
                 case OP_APUB: ok = vote(true) && apub(d.l); break;
