@@ -1010,13 +1010,18 @@ struct Consumer {
         const int hv = warp >> 2, dq = (warp & 3) * 8 + (lane & 7), pq = lane >> 3;
         float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
         const float* ph = pr + hv * kAttMax + pq * (kAttMax / 4);
+        const unsigned char* vr = vb + (size_t)pq * (kAttMax / 4) * 256 + dq * 8;
 #pragma unroll 8
         for (int j = 0; j < kAttMax / 4; j++) {
-            const int ix = pq * (kAttMax / 4) + j;
-            if (ix >= m_all) break;
+            if (pq * (kAttMax / 4) + j >= n) break;
             const float pj = ph[j];
-            const unsigned char* vr = ix < n ? vb + (size_t)ix * 256 : reinterpret_cast<const unsigned char*>(sh.vnew);
-            const uint2 vv = *reinterpret_cast<const uint2*>(vr + dq * 8);
+            const uint2 vv = *reinterpret_cast<const uint2*>(vr + (size_t)j * 256);
+            const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
+            o0 = fmaf(pj, v01.x, o0), o1 = fmaf(pj, v01.y, o1), o2 = fmaf(pj, v23.x, o2), o3 = fmaf(pj, v23.y, o3);
+        }
+        if (with_new && pq == 0) {  // the newest position, from shared memory
+            const float pj = pr[hv * kAttMax + n];
+            const uint2 vv = *reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned char*>(sh.vnew) + dq * 8);
             const float2 v01 = b2::h2_to_f2(vv.x), v23 = b2::h2_to_f2(vv.y);
             o0 = fmaf(pj, v01.x, o0), o1 = fmaf(pj, v01.y, o1), o2 = fmaf(pj, v23.x, o2), o3 = fmaf(pj, v23.y, o3);
         }
