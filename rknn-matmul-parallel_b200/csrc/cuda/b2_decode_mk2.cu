@@ -112,12 +112,15 @@ struct Sh {
     float mrg_o[NC][kGq][kHD];             // ... and output
     float act[kMaxCh];          // FP16-rounded SiLU(gate) * up of this CTA's channels
     float xres[kMaxH];          // x (layer input: the h_mid residual), then h_mid (the x residual)
-    __half xs[2][kMaxF];        // staged FP16 inputs: [0] q|k|v and lm_head, [1] gate|up
+    __half xs[2][kMaxH];        // staged FP16 inputs: [0] q|k|v and lm_head, [1] gate|up
     __half xo[kGq * kHD];       // attention output of the unit (o_proj input)
     B2MkLayer lay[kMaxLayers];  // the per-layer pointer table (read by every operation)
 };
 
-constexpr int kRing = 184 * 1024;
+constexpr int kRing = 192 * 1024;
+// an operation never wraps around the ring end, so any operation must fit
+// beside the largest wasted tail: twice the largest operation
+static_assert(2 * kOpMax <= kRing, "ring smaller than two operations");
 constexpr size_t kSmemBytes = (size_t)kRing + sizeof(Sh) + 128;
 static_assert(kSmemBytes <= 232448, "dynamic shared memory above the 227 KB per-block limit");
 
