@@ -392,7 +392,7 @@ size_t b2_mk_smem_bytes(void);
  * of the next phase.  The consumer warps take the stream in order and split
  * every 16-row tile's dot products over their K ranges.  Attention and o_proj
  * run fused per (kv head, row slice) unit: up to 240 cached positions every
- * unit attends over all of the head's positions; beyond, 8 units per kv head
+ * unit attends over all of the head's positions; beyond, 16 units per kv head
  * split them and publish partial softmax states that every unit of the head
  * merges.  The host routes contexts up to b2_mk2_max_context() cached
  * positions here (any length the cache holds). */

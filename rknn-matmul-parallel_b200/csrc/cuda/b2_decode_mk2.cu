@@ -11,42 +11,45 @@
 // turns the CTA's share of the token into a stream of operations kept in
 // shared-memory slots.  A data operation carries a block of weights — whole
 // 16-row tiles in the tile-major layout b2_tile_relayout writes, or K/V rows
-// of one kv head — copied into a byte ring by bulk copies whose completion is
-// counted on the slot's mbarrier.  A control operation has no data: it stages
-// the input of the next phase (wait for the previous phase, gather, RMSNorm,
-// FP16 rounding) or closes a phase.  The producer never waits for another
-// CTA, only for ring space, so it streams the next phases' weights while the
-// consumers wait on the dependency chain.
+// of one kv head — copied into a 192 KB byte ring by bulk copies whose
+// completion is counted on the slot's mbarrier.  A control operation has no
+// data.  The producer never waits for another CTA, only for ring space, so it
+// streams the next phases' weights while the consumers wait on the
+// dependency chain.
 //
-// The eight consumer warps take the operations in order.  A data operation's
+// The eight consumer warps take the operations in order.  A dot operation's
 // tiles are split over the warps by K range (each warp a slice of every
 // tile's 64-byte super-blocks; FP16 x FP16 products accumulated in FP32 with
 // the mixed-precision FMA); the partial sums meet in shared memory after one
-// barrier.  Every
-// barrier on this path is a vote, so a failed wait anywhere turns into a
-// failed vote and the whole CTA stops together.
+// barrier.  Every barrier on this path is a vote, so a failed wait anywhere
+// turns into a failed vote and the whole CTA stops together.
 //
-// Per layer l (the phases other CTAs depend on):
-//   XIN(l)   poll the layer-(l-1) output words (LL words: an FP32 value and
-//            a tag of step and layer in one 64-bit store, which readers poll); RMSNorm
-//            -> FP16 rows input
-//   QKV      tiles of q|k|v rows; results published as LL words
+// Per layer l (the steps other CTAs depend on; the steps in brackets run at
+// the start or end of the neighbouring data operation):
+//   QKV      [XIN: poll the layer-(l-1) output words (LL words: an FP32 value
+//            and a tag of step and layer in one 64-bit store, which readers
+//            poll); RMSNorm -> FP16] tiles of q|k|v rows; results published
+//            as LL words
 //   unit (kv head g, o_proj row slice r), on nkv * (G / nkv) CTAs:
-//     AIN    poll the q|k|v words of head group g; q/k RMSNorm, RoPE; unit r = 0
-//            appends the new K/V row to the cache
-//     KV     cached positions of head g, online softmax per warp
-//     AOUT   the newest position, merge of the warps, FP16 attention output
+//     KV     [AIN: poll the q|k|v words of head group g; q/k RMSNorm, RoPE;
+//            unit r = 0 appends the new K/V row to the cache] up to 120
+//            cached positions of head g in one two-pass softmax step over
+//            all consumer threads, the newest position folded into the last
+//            one [AOUT: FP16 attention output]; above 240 cached positions
+//            16 units per head split the positions [APUB: publish the
+//            partial state] and AMRG merges the 16 states per unit
 //     O      o_proj tiles of rows in slice r, columns of group g: partial sums
 //            published as LL words (one partial per kv head and output)
-//   RO       reducer: for the ~hidden/G outputs this CTA owns, the nkv
-//            partials in head order plus the residual x -> h_mid words
-//   GIN(l)   poll every h_mid word; RMSNorm(h_mid) -> FP16
+//   RO       reducer: for the 8 outputs this CTA owns, the nkv partials in
+//            head order plus the residual x -> h_mid words, then
+//            GIN: poll every h_mid word; RMSNorm(h_mid) -> FP16
 //   GU       tiles of 8 channels (gate and up rows interleaved): SiLU(g) * u
-//   DN       the same channels' rows of the input-major down weight times
-//            SiLU(g) * u: a partial of every output
-//   DEND     the CTA's down partial of every output as LL words
-//   RD       reducer: for the outputs this CTA owns, every CTA's partial in
-//            CTA order plus the residual h_mid -> layer-output words
+//   DN       [a barrier: every act is in] the same channels' rows of the
+//            input-major down weight times SiLU(g) * u: a partial of every
+//            output [DEND: the partial as LL words, one counter increment]
+//   RD       reducer: once the counter shows every CTA, for the 8 outputs this
+//            CTA owns every CTA's partial in CTA order plus the residual
+//            h_mid -> layer-output words
 // then LIN / LM / LEND (final norm, lm_head tiles, argmax keys) and the
 // last CTA to finish publishes the token.
 //
