@@ -409,8 +409,13 @@ def run_single_stream(args, world, rank, local):
         "config": single_stream_config(args.workload, m["ctx0"], quant, world),
         "roofline": roof,
         "clocks": m["clocks"],
+        # bytes a step_token call moves: the persistent kernels take 4 ints of
+        # step state and return the error flag and the token; the graph path
+        # uploads its parameter block (8 ints + an embedding row) and reads
+        # the token
         "e2e": {"value": round(world * K / m["e2e_s"], 2), "unit": "tok/s",
-                "h2d_bytes_per_step": 4 * (8 + shape.hidden_dim), "d2h_bytes_per_step": 4,
+                "h2d_bytes_per_step": 16 if m["persistent"] else 4 * (8 + shape.hidden_dim),
+                "d2h_bytes_per_step": 8 if m["persistent"] else 4,
                 "api": "matmul_decoder_step_token (C ABI)"},
         "gpu_launches": launches_per_token * K,
         "tokens_check": [int(t) for t in m["toks"][:4]],

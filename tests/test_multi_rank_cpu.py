@@ -76,3 +76,66 @@ def test_shard_sequences_balances_context(world):
     load = [int(sum(lens[i] for i in p)) for p in parts]
     assert max(load) - min(load) <= int(lens.max())  # greedy longest-first bound
     assert all(len(p) > 0 for p in parts)
+
+
+# ── vocab-sharded lm_head: the argmax-key protocol of
+# matmul_decoder_batch_shard_vocab (csrc/host/md_batch.c), on gloo ranks ──
+# Each rank holds a contiguous slice of the vocabulary.  Its best key per row
+# is (orderable(logit) << 32) | (0xFFFFFFFF - global index); an all-reduce MAX
+# of the keys over the ranks picks the largest logit and, on ties, the lowest
+# global index: the first maximum of the reference argmax
+# (src/cpu_ops.c:575-586).  NaN is ordered below every number.
+
+def _order(v: np.ndarray) -> np.ndarray:
+    u = v.astype(np.float32).view(np.uint32).astype(np.uint64)
+    out = np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    return np.where(np.isnan(v), 0, out).astype(np.uint64)
+
+
+def _keys(logits: np.ndarray, offset: int) -> np.ndarray:
+    idx = np.arange(logits.shape[1], dtype=np.uint64) + np.uint64(offset)
+    k = (_order(logits) << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - idx)
+    return k.max(axis=1)
+
+
+def _vocab_rank(rank: int, world: int, port: int, logits: np.ndarray, q) -> None:
+    try:
+        import torch
+        import torch.distributed as dist
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        V = logits.shape[1]
+        lo, hi = rank * V // world, (rank + 1) * V // world
+        k = torch.from_numpy(_keys(logits[:, lo:hi], lo).view(np.int64))  # same bits, signed view
+        # MAX over unsigned keys via the signed view: flip the top bit first
+        k ^= torch.tensor(np.int64(-0x8000000000000000))
+        dist.all_reduce(k, op=dist.ReduceOp.MAX)
+        k ^= torch.tensor(np.int64(-0x8000000000000000))
+        toks = (np.uint64(0xFFFFFFFF) - (k.numpy().view(np.uint64) & np.uint64(0xFFFFFFFF))).astype(np.int64)
+        dist.destroy_process_group()
+        q.put((rank, toks.tolist(), None))
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+def test_vocab_shard_argmax_keys_over_gloo_ranks():
+    pytest.importorskip("torch")
+    rng = np.random.default_rng(8)
+    logits = rng.standard_normal((6, 1000)).astype(np.float32)
+    logits[1, [10, 600]] = 9.0        # tie across the two slices: the lower index wins
+    logits[2, [700, 900]] = 9.0       # tie inside one slice
+    logits[3, 0] = np.nan             # NaN never wins
+    logits[4, :] = -3.0               # all equal: index 0
+    logits[5, 999] = 50.0
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_vocab_rank, args=(r, world, port, logits, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r, toks, err in res:
+        assert err is None, err
+        want = [int(np.nanargmax(np.where(np.isnan(row), -np.inf, row))) for row in logits]
+        assert toks == want, (r, toks, want)
