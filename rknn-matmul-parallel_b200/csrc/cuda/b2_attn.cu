@@ -685,9 +685,13 @@ extern "C" int b2_attention_blocks(float* out, uint16_t* out16, const float* q, 
 // (mma.sync m16n8k16, FP16 operands, FP32 accumulation) in the register
 // layout of FlashAttention-2 (Dao, 2023): each warp owns whole query rows, so
 // the online softmax needs only quad shuffles, and the score accumulators
-// become the A operand of P.V without leaving registers.  K and V blocks of 64
-// positions are double-buffered in shared memory with cp.async; rows are
-// padded by 16 bytes so ldmatrix reads are conflict-free.  Q and P are
+// become the A operand of P.V without leaving registers.  Two groups of four
+// warps own the same query rows and take alternate K/V blocks of 64 positions
+// (even / odd), each double-buffering its blocks in shared memory with
+// cp.async; at the end group 1 leaves its softmax state in shared memory and
+// group 0 merges it.  The causal triangle gives the last rows 8 blocks at
+// M = 512, so splitting them over two groups halves the longest CTA.  Rows
+// are padded by 16 bytes so ldmatrix reads are conflict-free.  Q and P are
 // rounded to FP16 (the reference keeps them FP32; the difference is far
 // inside the parity tolerance, see the prefill tests).
 
@@ -696,7 +700,8 @@ namespace {
 constexpr int kFaRows = 32;            // tokens per CTA
 constexpr int kFaKv = 64;              // positions per K/V block
 constexpr int kFaPad = kHD + 8;        // padded row (halves)
-constexpr int kFaThreads = 128;
+constexpr int kFaGroups = 2;           // warp groups splitting the K/V blocks
+constexpr int kFaThreads = 128 * kFaGroups;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -723,11 +728,12 @@ template <int G>
 __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __restrict__ out, __half* __restrict__ out16,
                                                                    const float* __restrict__ q, int ldq, int M, int nq,
                                                                    B2KVRef kv, int base) {
-    static_assert(G * kFaRows == 64, "four warps of 16 query rows");
+    static_assert(G * kFaRows == 64, "four warps of 16 query rows per group");
     extern __shared__ __align__(16) unsigned char fsm[];
     __half* sq = reinterpret_cast<__half*>(fsm);                 // [64][kFaPad]
-    __half* skv = sq + 64 * kFaPad;                               // [2 buffers][K, V][kFaKv][kFaPad]
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 7, gtid = tid & 127, warp = (tid >> 5) & 3;
+    // this group's [2 buffers][K, V][kFaKv][kFaPad]
+    __half* skv = sq + 64 * kFaPad + (size_t)grp * 4 * kFaKv * kFaPad;
     const int m0 = blockIdx.x * kFaRows, g = blockIdx.y;
     const int last = base + M - 1;                                // last filled cache position
     const int pmax = min(last, base + m0 + kFaRows - 1);          // last position any row of the CTA attends
@@ -751,7 +757,7 @@ __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __rest
     auto load_block = [&](int blk, int buf) {
         __half* dk = skv + (size_t)buf * 2 * kFaKv * kFaPad;
         __half* dv = dk + kFaKv * kFaPad;
-        for (int i = tid; i < kFaKv * (kHD / 8); i += kFaThreads) {
+        for (int i = gtid; i < kFaKv * (kHD / 8); i += 128) {
             const int r = i / (kHD / 8), c = (i % (kHD / 8)) * 8;
             const int p = min(blk * kFaKv + r, pmax);  // rows past pmax repeat it (masked below)
             cp_async16(dk + r * kFaPad + c, kg + (size_t)p * kHD + c);
@@ -759,7 +765,9 @@ __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __rest
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    load_block(0, 0);
+    auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory"); };
+    if (grp < nblk) load_block(grp, 0);
+    __syncthreads();  // Q rows staged for both groups
 
     const int g8 = lane >> 2, q4 = lane & 3;
     // the two query rows of this lane: warp rows 16 warp + g8 and + 8
@@ -771,15 +779,15 @@ __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __rest
 #pragma unroll
     for (int j = 0; j < kHD / 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
-    for (int blk = 0; blk < nblk; blk++) {
-        if (blk + 1 < nblk) {
-            load_block(blk + 1, (blk + 1) & 1);
+    for (int blk = grp, it = 0; blk < nblk; blk += kFaGroups, it++) {
+        if (blk + kFaGroups < nblk) {
+            load_block(blk + kFaGroups, (it + 1) & 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        __syncthreads();
-        const __half* sk = skv + (size_t)(blk & 1) * 2 * kFaKv * kFaPad;
+        group_sync();
+        const __half* sk = skv + (size_t)(it & 1) * 2 * kFaKv * kFaPad;
         const __half* sv = sk + kFaKv * kFaPad;
         // S = Q K^T for this warp's 16 rows x 64 positions
         float s[kFaKv / 8][4];
@@ -862,7 +870,35 @@ __global__ void __launch_bounds__(kFaThreads) flash_prefill_kernel(float* __rest
                 mma_f16(o[j + 1], a, b[2], b[3]);
             }
         }
-        __syncthreads();  // the buffer is refilled two blocks later
+        group_sync();  // the buffer is refilled two blocks later
+    }
+    // group 1 hands its state to group 0 through its (now idle) K/V buffers:
+    // [warp][lane][mA, mB, lA, lB, o[16][4]]
+    constexpr int kSt = 4 + 4 * (kHD / 8);
+    float* st = reinterpret_cast<float*>(sq + 64 * kFaPad + 4 * kFaKv * kFaPad) + (size_t)(warp * 32 + lane) * kSt;
+    if (grp == 1) {
+        st[0] = mA, st[1] = mB, st[2] = lA, st[3] = lB;
+#pragma unroll
+        for (int j = 0; j < kHD / 8; j++)
+            *reinterpret_cast<float4*>(st + 4 + 4 * j) = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+    }
+    __syncthreads();
+    if (grp == 1) return;
+    {
+        const float m1A = st[0], m1B = st[1], l1A = st[2], l1B = st[3];
+        const float nA = fmaxf(mA, m1A), nB = fmaxf(mB, m1B);
+        const float a0 = mA == -INFINITY ? 0.f : expf(mA - nA), a1 = m1A == -INFINITY ? 0.f : expf(m1A - nA);
+        const float b0 = mB == -INFINITY ? 0.f : expf(mB - nB), b1 = m1B == -INFINITY ? 0.f : expf(m1B - nB);
+        lA = lA * a0 + l1A * a1;
+        lB = lB * b0 + l1B * b1;
+#pragma unroll
+        for (int j = 0; j < kHD / 8; j++) {
+            const float4 u = *reinterpret_cast<const float4*>(st + 4 + 4 * j);
+            o[j][0] = o[j][0] * a0 + u.x * a1;
+            o[j][1] = o[j][1] * a0 + u.y * a1;
+            o[j][2] = o[j][2] * b0 + u.z * b1;
+            o[j][3] = o[j][3] * b0 + u.w * b1;
+        }
     }
     // out[m][(g*G + h) * 128 + d] = O / l
     const int tA = rA % kFaRows, tB = rB % kFaRows;
@@ -891,7 +927,7 @@ extern "C" int b2_attention_prefill(float* out, uint16_t* out16, const float* q,
     if (hd != kHD || (!out && !out16) || !q || !kv || nkv <= 0 || nq != 2 * nkv || base < 0 || base + M > kv->max_seq ||
         ldq % 4 || kv->rows_seq)
         return b2_set_error(B2_ERR_INVALID_ARG, "b2_attention_prefill: needs hd 128, GQA group 2, one sequence");
-    const size_t smem = (size_t)(64 + 4 * kFaKv) * kFaPad * sizeof(__half);
+    const size_t smem = (size_t)(64 + 4 * kFaGroups * kFaKv) * kFaPad * sizeof(__half);
     static int configured = 0;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
