@@ -6,6 +6,7 @@ workloads (Qwen3-0.6B: hidden 1024, 16 q / 8 kv heads of 128, ffn 3072).
     python rknn-matmul-parallel_b200/python/kernel_bench.py gemm-gu     [--rows 64] [--wtype i4] [--split 0]
     (gemm-qkv, gemm-o, gemm-down likewise)
     python rknn-matmul-parallel_b200/python/kernel_bench.py log-mel     [--seconds 30]
+    python rknn-matmul-parallel_b200/python/kernel_bench.py sample      [--top-k 50] [--top-p 0.9]
 
 Attention rows are independent sequences whose cache lengths are drawn
 uniformly from [128, 4096) (the batched-decode workload, seeded); GEMM
@@ -14,7 +15,8 @@ a 256 MB write that flushes L2; the line printed per case gives the median
 and minimum device time (CUDA events around the C-ABI call) and the
 algorithmic bytes (weights, or the K and V rows attended) per microsecond;
 for log-mel (the ASR front end) the FLOPs of the direct 400-point DFT and
-the mel product per second.
+the mel product per second; for sample (on-device sampling over the 151936
+logits of one token) the logit bytes read per second.
 Every kernel runs through the library's C-ABI (libmatmul_decoder.so)."""
 from __future__ import annotations
 
@@ -41,7 +43,9 @@ WTYPES = {"f16": (bd.W_F16, 2.0), "i8": (bd.W_I8, 1.0), "i4": (bd.W_I4, 0.5)}
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("kernel", choices=["attn-blocks", "attn-split", "log-mel"] + sorted(GEMMS))
+    ap.add_argument("kernel", choices=["attn-blocks", "attn-split", "log-mel", "sample"] + sorted(GEMMS))
+    ap.add_argument("--top-k", type=int, default=50, help="sample: top_k (0: all)")
+    ap.add_argument("--top-p", type=float, default=0.9, help="sample: top_p")
     ap.add_argument("--seconds", type=float, default=30.0, help="log-mel: audio length at 16 kHz")
     ap.add_argument("--rows", type=int, default=64, help="token rows (sequences for attention)")
     ap.add_argument("--wtype", choices=sorted(WTYPES), default="i4")
@@ -62,7 +66,21 @@ def main() -> int:
     M = a.rows
     keep = []
 
-    if a.kernel == "log-mel":
+    if a.kernel == "sample":
+        V = 151936
+        logits = torch.randn(V, device=dev) * 3.0
+        rep = torch.from_numpy(rng.integers(0, V, 64).astype(np.int32)).to(dev)
+        tok = torch.zeros(8, dtype=torch.int32, device=dev)
+        keep += [logits, rep, tok]
+        nbytes = V * 4.0
+        label = f"sample V={V} top_k={a.top_k} top_p={a.top_p} temperature=0.8 penalty=1.1 (64 repeat tokens)"
+        counter = [0]
+
+        def run():
+            counter[0] += 1
+            bd.check(lib.b2_sample_token(logits.data_ptr(), V, rep.data_ptr(), 64, 1.1, a.top_k, a.top_p, 0.8, 7,
+                                         counter[0], tok.data_ptr(), None, stream), a.kernel)
+    elif a.kernel == "log-mel":
         n = int(a.seconds * 16000)
         audio = torch.from_numpy((0.1 * rng.standard_normal(n)).astype(np.float32)).to(dev)
         filt = torch.from_numpy(rng.random((201, 128), dtype=np.float32) * 0.01).to(dev)
