@@ -9,7 +9,8 @@
 //   2. top_k == 1: the first index of the largest x (no temperature)
 //   3. v = x / temperature (IEEE division; temperature <= 0 means 1)
 //   4. the K = top_k largest v (all when top_k <= 0 or > V), ordered by v
-//      descending and index ascending; w_i = exp(v_i - v_max) in double
+//      descending and index ascending; w_i = exp(v_i - v_max), the
+//      exponential in FP32 and every sum of weights in FP64
 //   5. top_p in (0, 1): keep the shortest prefix of that order whose mass
 //      reaches top_p of the K-set's mass
 //   6. draw a token from the kept set with probability w_i / sum(w)
@@ -38,10 +39,17 @@ constexpr int kCl = 8;                    // CTAs of the cluster
 constexpr int kT = 1024;                  // threads per CTA
 constexpr int kW = kT / 32;
 constexpr int kMaxSlice = 54 * 1024;      // vocabulary entries per CTA (216 KB)
+// Histogram masses are summed as 64-bit fixed point (weights <= 1 times
+// 2^40; 2^18 entries cannot overflow): integer shared-memory atomics, where
+// FP64 ones contended on the few busiest digits, and sums that do not depend
+// on the order of the additions.
+constexpr double kMassOne = 1099511627776.0;  // 2^40
 
 struct Shared {
     unsigned int hist[2][256];            // radix counts (double-buffered across rounds)
-    double mass[2][256];                  // radix masses
+    unsigned long long mass[2][256];      // radix masses, fixed point (kMassOne = 1.0)
+    unsigned int tot[256];                // cluster-wide counts of the current round
+    double totm[256];                     // cluster-wide masses of the current round
     unsigned long long wkey[kW];          // warp partials of (key, index) maxima
     unsigned long long wkey2[kW];
     double wd[kW];                        // warp partials of doubles
@@ -66,6 +74,14 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
     return z ^ (z >> 31);
+}
+
+// Weight of a logit: exp(v - v_max) in FP32 (the FP64 exponential made the
+// radix rounds FP64-bound on the cluster's 8 SMs), summed in FP64 by callers.
+// (A NaN logit weighs nothing.)
+__device__ __forceinline__ double wgt(float v, float vmax) {
+    const float e = expf(v - vmax);
+    return e == e ? (double)e : 0.0;
 }
 
 // Block-wide sums / maxima with every thread receiving the result.
@@ -197,17 +213,24 @@ struct Ctx {
             if ((u & mask) == prefix && sel(i, u)) atomicAdd(&sh.hist[buf][(u >> shift) & 255u], 1u);
         }
         cl.sync();  // every CTA's histogram complete
+        if (threadIdx.x < 256) {  // one digit per thread, the 8 remote reads in flight together
+            unsigned int v[kCl];
+#pragma unroll
+            for (unsigned c = 0; c < kCl; c++) v[c] = cl.map_shared_rank(&sh.hist[buf][0], c)[threadIdx.x];
+            unsigned int t = 0;
+#pragma unroll
+            for (unsigned c = 0; c < kCl; c++) t += v[c];
+            sh.tot[threadIdx.x] = t;
+        }
+        __syncthreads();
         if (threadIdx.x < 32) {
-            // lane l sums digits 255 - 8 l .. 248 - 8 l over the cluster
+            // lane l takes digits 255 - 8 l .. 248 - 8 l
             const int lane = threadIdx.x;
             unsigned int c8[8], s = 0;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int d = 255 - 8 * lane - j;
-                unsigned int t = 0;
-                for (unsigned c = 0; c < kCl; c++) t += cl.map_shared_rank(&sh.hist[buf][0], c)[d];
-                c8[j] = t;
-                s += t;
+                c8[j] = sh.tot[255 - 8 * lane - j];
+                s += c8[j];
             }
             unsigned int inc = s;
 #pragma unroll
@@ -242,26 +265,34 @@ struct Ctx {
 
     // Same with masses: the digit where the running mass first reaches want.
     template <class Sel>
-    __device__ unsigned int mass_round(int buf, int shift, uint32_t prefix, uint32_t mask, double want, double vmax,
+    __device__ unsigned int mass_round(int buf, int shift, uint32_t prefix, uint32_t mask, double want, float vmax,
                                        double& above, Sel sel) {
-        for (int i = threadIdx.x; i < 256; i += kT) sh.mass[buf][i] = 0.0;
+        for (int i = threadIdx.x; i < 256; i += kT) sh.mass[buf][i] = 0ull;
         __syncthreads();
         for (int i = r0; i < r1; i++) {
             const uint32_t u = b2::float_order(v[i]);
             if ((u & mask) == prefix && sel(i, u))
-                atomicAdd(&sh.mass[buf][(u >> shift) & 255u], exp((double)v[i] - vmax));
+                atomicAdd(&sh.mass[buf][(u >> shift) & 255u],
+                          (unsigned long long)__double2ll_rn(wgt(v[i], vmax) * kMassOne));
         }
         cl.sync();
+        if (threadIdx.x < 256) {
+            unsigned long long v[kCl];
+#pragma unroll
+            for (unsigned c = 0; c < kCl; c++) v[c] = cl.map_shared_rank(&sh.mass[buf][0], c)[threadIdx.x];
+            unsigned long long t = 0ull;
+#pragma unroll
+            for (unsigned c = 0; c < kCl; c++) t += v[c];
+            sh.totm[threadIdx.x] = (double)t / kMassOne;
+        }
+        __syncthreads();
         if (threadIdx.x < 32) {
             const int lane = threadIdx.x;
             double m8[8], s = 0.0;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int d = 255 - 8 * lane - j;
-                double t = 0.0;
-                for (unsigned c = 0; c < kCl; c++) t += cl.map_shared_rank(&sh.mass[buf][0], c)[d];
-                m8[j] = t;
-                s += t;
+                m8[j] = sh.totm[255 - 8 * lane - j];
+                s += m8[j];
             }
             double inc = s;
 #pragma unroll
@@ -364,7 +395,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kT, 1)
     for (int i = threadIdx.x; i < n; i += kT) v[i] = __fdiv_rn(v[i], temp);
     __syncthreads();
     const unsigned long long kmax = cluster_argmax(c);
-    const double vmax = (double)key_value((uint32_t)(kmax >> 32));
+    const float vmaxf = key_value((uint32_t)(kmax >> 32));
     const unsigned int K = (top_k <= 0 || top_k > V) ? (unsigned)V : (unsigned)top_k;
 
     // ── top-K threshold: key T and how many entries equal to T (lowest
@@ -403,7 +434,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kT, 1)
         unsigned int seen = 0;
         for (int i = c.r0; i < c.r1; i++) {
             const uint32_t u = b2::float_order(v[i]);
-            if (in_k(u, seen)) mine += exp((double)v[i] - vmax);
+            if (in_k(u, seen)) mine += wgt(v[i], vmaxf);
             seen += u == T;
         }
     }
@@ -423,13 +454,13 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kT, 1)
             // entries of the K-set: by key, except the ties at T (resolved
             // below), which are all counted; a cut at key T keeps at most needT
             const auto sel = [&](int, uint32_t u) { return K >= (unsigned)V || u >= T; };
-            const unsigned int d = c.mass_round(r & 1, shift, prefix, mask, want - above_total, vmax, above, sel);
+            const unsigned int d = c.mass_round(r & 1, shift, prefix, mask, want - above_total, vmaxf, above, sel);
             above_total += above;
             prefix |= d << shift;
             mask |= 255u << shift;
         }
         P = prefix;
-        const double w = exp((double)key_value(P) - vmax);
+        const double w = wgt(key_value(P), vmaxf);
         // smallest j with above_total + j w >= want
         double j = w > 0.0 ? ceil((want - above_total) / w) : 1.0;
         j = j < 1.0 ? 1.0 : j;
@@ -451,7 +482,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kT, 1)
         for (int i = c.r0; i < c.r1; i++) {
             const uint32_t u = b2::float_order(v[i]);
             if (kept(u, seen)) {
-                wm += exp((double)v[i] - vmax);
+                wm += wgt(v[i], vmaxf);
                 nk++;
                 last = i;
             }
@@ -479,7 +510,7 @@ __global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kT, 1)
         for (int i = c.r0; i < c.r1; i++) {
             const uint32_t u = b2::float_order(v[i]);
             if (kept(u, seen)) {
-                acc += exp((double)v[i] - vmax);
+                acc += wgt(v[i], vmaxf);
                 if (r < acc) {
                     at = i;
                     break;
