@@ -679,7 +679,7 @@ int matmul_decoder_step_sample(MatmulDecoderContext* ctx, int token_id, const fl
     if (!ctx->d_sample || ctx->d_sample_cap < n_rep) {
         if (ctx->d_sample) b2_free(ctx->d_sample);
         ctx->d_sample = NULL;
-        const int cap = n_rep > 256 ? n_rep : 256;
+        const int cap = 2 * n_rep > 256 ? 2 * n_rep : 256;  /* room to grow with a generation's history */
         if ((rc = b2_malloc((void**)&ctx->d_sample, (size_t)(8 + cap) * 4))) return fail("sampler buffer", rc);
         ctx->d_sample_cap = cap;
     }

@@ -185,20 +185,17 @@ class PyMatmulDecoder {
             int rc = matmul_decoder_step(ctx_, prompt_tokens[i], nullptr, nullptr);
             if (rc < 0) throw std::runtime_error("generate: prompt step failed " + std::to_string(rc));
         }
-        const bool greedy = top_k == 1 && repeat_penalty == 1.0f;
-        std::vector<float> logits(greedy ? 0 : cfg_.vocab_size);
         int tok = prompt_tokens.back();
         for (int i = 0; i < max_new_tokens; i++) {
+            // the token is drawn on the device (greedy: the argmax), with the
+            // prompt and the tokens so far as the repeat-penalty list; no
+            // logits are copied to the host
+            p.repeat_tokens = history.data();
+            p.n_repeat_tokens = (int)history.size();
             int next;
-            if (greedy) {
-                next = matmul_decoder_step_token(ctx_, tok, nullptr);
-            } else {
-                next = matmul_decoder_step(ctx_, tok, nullptr, logits.data());
-                if (next >= 0) {
-                    p.repeat_tokens = history.data();
-                    p.n_repeat_tokens = (int)history.size();
-                    next = matmul_sample_token(logits.data(), cfg_.vocab_size, &p);
-                }
+            {
+                py::gil_scoped_release nogil;
+                next = matmul_decoder_step_sample(ctx_, tok, nullptr, &p);
             }
             if (next < 0) throw std::runtime_error("generate: step failed " + std::to_string(next));
             out.push_back(next);
